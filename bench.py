@@ -1,0 +1,390 @@
+"""SBDA attention fwd+bwd benchmark on B200 (BASELINE.json metric, config 4).
+
+Workload: one 1,048,576-position sequence per GPU, 20 SBDA layers (offsets
+(0,1), (0,2), (0,1,2,4) ... (0,1,2,2^19)), 4 heads x 64, bf16, q/k/v/dO ~ N(0,1)
+from a seed, in the reference's memory layout ([B,L,H,D] projections viewed
+as [B,H,L,D]).  A step is the forward of all 20 layers followed by the
+backward of all 20 layers.  Metric: Mpositions/s = positions per GPU x GPUs /
+step time.  Each tensor is 512 MiB (> 126 MB L2), so no L2 flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Under torchrun each rank runs an independent sequence (batch sharding, no
+data-path collective; weak scaling); the timed region is bracketed by a
+barrier and synchronize on every rank and the slowest rank's time is used.
+``--impl reference`` times the reference's algorithm (the CPU oracle port of
+``BiAttn/left_v2.py``'s exact path) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "SBDA attn fwd+bwd Mpositions/s at 1M×20L; % of B200 HBM roofline"
+UNIT = "Mpositions/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--length", type=int, default=1 << 20)
+    p.add_argument("--layers", type=int, default=20)
+    p.add_argument("--heads", type=int, default=4)
+    p.add_argument("--head-dim", type=int, default=64)
+    p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-sample-length", type=int, default=16384)
+    return p.parse_args()
+
+
+def workload_config(args, world: int) -> dict:
+    return {
+        "workload": (f"cfg4: SBDA attention stack fwd+bwd, {args.length} positions x {args.layers} layers, "
+                     f"{args.heads} heads x {args.head_dim}, batch 1 per GPU"),
+        "global_batch": world,
+        "seq_len": args.length,
+        "layers": args.layers,
+        "heads": args.heads,
+        "head_dim": args.head_dim,
+        "parallelism": f"batch-sharded x{world} (independent sequences, no collectives)",
+        "l2": "every tensor 512 MiB > 126 MB L2; no flush needed",
+    }
+
+
+def measured_peak_gbs() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as handle:
+            return float(json.load(handle)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic() -> float | None:
+    """Per-launch DRAM bytes of the backward kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "sbda_bwd_kernel_cfg4.md")
+    try:
+        with open(path) as handle:
+            for line in handle:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, RuntimeError):
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(args, *, sample_length: int, threads: int | None = None) -> dict:
+    """Oracle port of the reference's exact path (fp32, CPU) over all layers at a bounded length."""
+    from oracle import sbda_oracle as orc
+
+    if threads:
+        torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    shape = (1, args.heads, sample_length, args.head_dim)
+    q, k, v, do = (torch.randn(shape, generator=g) for _ in range(4))
+    orc.exact_attention_grads(q[:, :, :256], k[:, :, :256], v[:, :, :256], (0, 1, 2, 4), do[:, :, :256])
+    start = time.perf_counter()
+    for layer in range(1, args.layers + 1):
+        offsets = orc.schedule_offsets(layer, "sbda", args.layers)
+        orc.exact_attention_grads(q, k, v, offsets, do)
+    elapsed = time.perf_counter() - start
+    return {"value": sample_length / elapsed / 1e6, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": (f"oracle port of left_v2 exact path (torch CPU fp32), fwd+bwd of all {args.layers} "
+                       f"layers at {sample_length} positions x {args.heads} heads x {args.head_dim}; "
+                       "O(N) per layer, so positions/s carries to 1M"),
+            "seconds": elapsed}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import sbda_oracle as orc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = 2048
+    g = torch.Generator().manual_seed(7)
+    shape = (1, args.heads, sample, args.head_dim)
+    q, k, v, do = (torch.randn(shape, generator=g) for _ in range(4))
+    layer_offsets = [orc.schedule_offsets(layer, "sbda", args.layers) for layer in range(1, args.layers + 1)]
+
+    def step():
+        for offsets in layer_offsets:
+            orc.exact_attention_grads(q, k, v, offsets, do)
+
+    for _ in range(args.warmup):
+        step()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = (time.perf_counter() - start) / max(1, args.steps)
+    value = sample / elapsed / 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": (f"each step: oracle port of left_v2 exact path (torch CPU fp32), fwd+bwd of "
+                                    f"all {args.layers} layers at {sample} positions x {args.heads} heads x "
+                                    f"{args.head_dim}; the reference ships no native CPU code")},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args) -> None:
+    import torch.distributed as dist
+
+    import sbda_b200
+    from sbda_b200 import ops
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    L, H, D, layers = args.length, args.heads, args.head_dim, args.layers
+    dtype = torch.bfloat16
+    offsets = sbda_b200.sbda_layer_offsets(layers)
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+
+    def blhd():
+        return torch.randn((1, L, H, D), device=device, dtype=dtype, generator=gen).permute(0, 2, 1, 3)
+
+    qs = [blhd() for _ in range(layers)]
+    ks = [blhd() for _ in range(layers)]
+    vs = [blhd() for _ in range(layers)]
+    dos = [blhd() for _ in range(layers)]
+    lses = [torch.empty((1, H, L), device=device, dtype=torch.float32) for _ in range(layers)]
+    out = torch.empty_like(qs[0])
+    grads = (torch.empty_like(qs[0]), torch.empty_like(qs[0]), torch.empty_like(qs[0]))
+    fwd_events, bwd_events = [], []
+
+    def step(record: bool = False):
+        for layer in range(layers):
+            if record:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+            ops.sbda_forward(qs[layer], ks[layer], vs[layer], offsets[layer], out=out, lse=lses[layer])
+            if record:
+                e.record()
+                fwd_events.append((s, e))
+        for layer in reversed(range(layers)):
+            if record:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+            ops.sbda_backward(qs[layer], ks[layer], vs[layer], dos[layer], lses[layer], offsets[layer],
+                              grads=grads)
+            if record:
+                e.record()
+                bwd_events.append((s, e))
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if sbda_b200.device_status(reset=True):
+        raise RuntimeError("device fault reported during warm-up")
+
+    # Timed region: steps back to back, bracketed by barrier + synchronize.
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    step_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+
+    # Per-kernel durations (separate pass with an event pair around every launch).
+    for _ in range(2):
+        step(record=True)
+    torch.cuda.synchronize()
+    fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in fwd_events)
+    bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in bwd_events)
+
+    rows = H * L
+    e = 2
+    fwd_bytes = rows * (4 * D * e + 4)
+    bwd_bytes = rows * (7 * D * e + 4)
+    peak, peak_kind = measured_peak_gbs()
+    positions = L * world
+    value = positions / (step_ms * 1e-3) / 1e6
+    dominant = ("sbda_bwd_kernel", bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else ("sbda_fwd_kernel", fwd_bytes, fwd_ms)
+    achieved = dominant[1] / (dominant[2] * 1e-3) / 1e9
+    traffic = profiled_traffic() if dominant[0] == "sbda_bwd_kernel" else None
+    step_bytes = layers * (fwd_bytes + bwd_bytes)
+    step_gbs = step_bytes / (step_ms * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(args, device, offsets, barrier, max_over_ranks, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, sample_length=args.cpu_sample_length, threads=os.cpu_count())
+        cpu.pop("seconds", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded, resident in HBM",
+            "config": workload_config(args, world),
+            "roofline": {"bound": "hbm", "kernel": dominant[0], "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": dominant[1],
+                         "launch_ms": dominant[2]},
+            "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
+                              "algorithmic_bytes_per_step": step_bytes, "fwd_launch_ms": fwd_ms,
+                              "bwd_launch_ms": bwd_ms},
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": 2 * layers * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
+    """Public API (fused_sbda_key_backward + autograd) with pinned host buffers.
+
+    Every layer of every step copies q, k, v, dO host->device and dQ, dK, dV
+    device->host inside the timed region.
+    """
+    import sbda_b200
+
+    L, H, D, layers = args.length, args.heads, args.head_dim, args.layers
+    g = torch.Generator().manual_seed(99)
+    host_in = [torch.randn((1, L, H, D), generator=g).to(torch.bfloat16).pin_memory() for _ in range(4)]
+    host_out = [torch.empty((1, L, H, D), dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    dev_in = [torch.empty((1, L, H, D), device=device, dtype=torch.bfloat16) for _ in range(4)]
+    off_tensors = [torch.tensor(o, dtype=torch.int32, device=device) for o in offsets]
+
+    def step():
+        for layer in range(layers):
+            for dst, src in zip(dev_in, host_in):
+                dst.copy_(src, non_blocking=True)
+            q, k, v = (t.permute(0, 2, 1, 3).requires_grad_() for t in dev_in[:3])
+            out = sbda_b200.fused_sbda_key_backward(q, k, v, off_tensors[layer])
+            out.backward(dev_in[3].permute(0, 2, 1, 3))
+            for dst, src in zip(host_out, (q.grad, k.grad, v.grad)):
+                dst.copy_(src.permute(0, 2, 1, 3), non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    steps = max(1, args.e2e_steps)
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end) / steps)
+    tensor_bytes = L * H * D * 2
+    return {"value": L * world / (ms * 1e-3) / 1e6, "unit": UNIT, "h2d_bytes_per_step": 4 * tensor_bytes * layers,
+            "d2h_bytes_per_step": 3 * tensor_bytes * layers, "ms_per_step": ms, "steps": steps,
+            "api": "sbda_b200.fused_sbda_key_backward + autograd backward, pinned host buffers"}
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

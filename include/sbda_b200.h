@@ -1,0 +1,123 @@
+/*
+ * sbda_b200.h -- C ABI of the B200 (sm_100a) SBDA sparse gather-softmax
+ * attention kernels.
+ *
+ * SBDA (Staged Binary-Local Diffusion Attention) layer l lets query i attend
+ * to at most four exact causal sources i - o, o in O_l, with
+ * O_l = (0, 2^(l-1)) for l <= 2 and (0, 1, 2, 2^(l-1)) for l >= 3.
+ * Sources with i - o < 0 are masked; scale = head_dim^-0.5.
+ *
+ * These entry points replace the device work of the reference autograd op
+ * `fused_sbda_key_backward(q, k, v, offsets)` and of its native-GQA twin
+ * `fused_sbda_gqa_key_backward` (BiAttn/sbda_triton.py:1467-1493):
+ *
+ *   sbda_b200_forward   <- _FusedSBDAKeyBackward.forward      (sbda_triton.py:1294-1327)
+ *                          _FusedSBDAGQAKeyBackward.forward   (sbda_triton.py:1366-1400)
+ *   sbda_b200_backward  <- _FusedSBDAKeyBackward.backward     (sbda_triton.py:1330-1360)
+ *                          _FusedSBDAGQAKeyBackward.backward  (sbda_triton.py:1402-1434)
+ *
+ * The forward saves a fp32 log-sum-exp per query row instead of the
+ * reference's per-source weight table W[B,H,L,S]; the backward recomputes
+ * the weights from it.  Both are deterministic and use no atomics.
+ *
+ * Conventions
+ *  - Every tensor is a [B, H, L, D] view described by its data pointer and
+ *    four element strides (batch, head, position, channel).  q/out/grad_out/
+ *    grad_q have H heads; k/v/grad_k/grad_v have kv_heads heads
+ *    (H % kv_heads == 0; query head h reads kv head h / (H / kv_heads)).
+ *  - lse is a contiguous fp32 [B, H, L] buffer owned by the caller.
+ *  - offsets is a HOST array of n_offsets (1..4) distinct non-negative ints.
+ *    At most one offset may exceed the tile height (64); that one is the
+ *    "far" (dyadic) source, the rest are the "near" window.
+ *  - No entry point allocates device memory, synchronises, or keeps state
+ *    between calls.  Work is enqueued on `stream` (a cudaStream_t; NULL is
+ *    the legacy default stream).
+ *  - Return value: SBDA_OK or an error code; sbda_b200_status_string() names it.
+ */
+#ifndef SBDA_B200_H_
+#define SBDA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SBDA_B200_ABI_VERSION 1
+
+/* Element types (match the reference's accepted dtypes, sbda_triton.py:1302-1303). */
+enum sbda_dtype {
+  SBDA_DTYPE_F32 = 0,
+  SBDA_DTYPE_F16 = 1,
+  SBDA_DTYPE_BF16 = 2
+};
+
+/* Status codes.  The Python wrapper maps them onto the reference's exception
+ * types (sbda_triton.py:1295-1303): INVALID -> ValueError, DTYPE -> TypeError,
+ * UNSUPPORTED / CUDA / DEVICE -> RuntimeError. */
+enum sbda_status {
+  SBDA_OK = 0,
+  SBDA_ERR_INVALID = 1,      /* bad shape, stride, offsets or null pointer */
+  SBDA_ERR_DTYPE = 2,        /* unsupported element type */
+  SBDA_ERR_UNSUPPORTED = 3,  /* valid but outside the kernel's envelope (head_dim > 128, two far offsets) */
+  SBDA_ERR_CUDA = 4,         /* a CUDA runtime / driver call failed */
+  SBDA_ERR_DEVICE = 5        /* a kernel reported a device-side fault (bounded wait expired) */
+};
+
+/* A [B, H, L, D] view: element (0,0,0,0) and element strides. */
+typedef struct sbda_tensor {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_l;
+  int64_t stride_d;
+} sbda_tensor;
+
+/* Problem shape shared by forward and backward. */
+typedef struct sbda_shape {
+  int64_t batch;
+  int64_t heads;     /* query heads H */
+  int64_t kv_heads;  /* key/value heads; == heads for MHA */
+  int64_t length;    /* sequence positions L */
+  int64_t head_dim;  /* D, 1..128 */
+} sbda_shape;
+
+/* Library ABI version (SBDA_B200_ABI_VERSION). */
+int sbda_b200_abi_version(void);
+
+/* Human-readable name of a status code (static string). */
+const char* sbda_b200_status_string(int status);
+
+/*
+ * Forward.  out[b,h,i,:] = sum_s p_s v[b,h/G,i-o_s,:] with
+ * p = softmax_s(scale * <q[b,h,i,:], k[b,h/G,i-o_s,:]>) over valid sources,
+ * lse[b,h,i] = log sum_s exp(score_s) (natural log; -inf if no source is valid).
+ * out has q's dtype; math is fp32.
+ */
+int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                      float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                      sbda_tensor out, float* lse, void* stream);
+
+/*
+ * Backward (gather form).  Given the forward inputs, lse and grad_out, writes
+ * grad_q, grad_k, grad_v (each exactly once, in the input dtype).  grad_k and
+ * grad_v sum over the H / kv_heads query heads that share a kv head.
+ */
+int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                       float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                       sbda_tensor grad_out, const float* lse,
+                       sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v,
+                       void* stream);
+
+/*
+ * Reads (and, if reset != 0, clears) the calling device's fault word that
+ * kernels set instead of trapping (bit 0: a bounded wait on a tensor-copy
+ * barrier expired).  Synchronous: waits for the device.  Not for hot paths.
+ */
+int sbda_b200_device_status(uint32_t* flags_out, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SBDA_B200_H_ */

@@ -1,0 +1,34 @@
+"""SBDA sparse gather-softmax attention for NVIDIA B200 (sm_100a).
+
+Import as ``sbda_b200`` (the repository root's ``sbda_b200.py`` maps that
+name onto this directory).  The compute runs in ``libsbda_b200.so`` (built
+from ``csrc/`` by ``build.py``) behind the C ABI of ``include/sbda_b200.h``.
+"""
+
+from .ops import (
+    device_status,
+    fused_sbda,
+    fused_sbda_block,
+    fused_sbda_block_full,
+    fused_sbda_gqa_key_backward,
+    fused_sbda_key_backward,
+    host_offsets,
+    sbda_backward,
+    sbda_forward,
+)
+from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_offsets
+
+__all__ = [
+    "PATH_TOPOLOGIES", "SBDAttention", "SBDAAttention", "device_status", "fused_sbda",
+    "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
+    "fused_sbda_key_backward", "host_offsets", "sbda_backward", "sbda_forward",
+    "sbda_layer_offsets", "sbda_stage", "topology_offsets",
+]
+
+
+def __getattr__(name: str):
+    if name in ("SBDAttention", "SBDAAttention"):
+        from .attention import SBDAttention
+
+        return SBDAttention
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

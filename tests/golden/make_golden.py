@@ -1,0 +1,136 @@
+"""Generate golden vectors by running the reference's own SBDA code on the CPU.
+
+Run from the repository root with the reference checkout available::
+
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
+
+It imports ``BiAttn`` from the reference, builds ``SBDAttention`` modules on
+the exact (non-fused) path -- the path the reference itself takes on the CPU
+(``BiAttn/left_v2.py:263-267`` requires ``x.is_cuda`` for the fused route) --
+and records, for seeded inputs:
+
+* the module input ``x``, its parameters and the module output,
+* the post-RMSNorm/RoPE ``q``/``k`` and the ``v`` that reach the gather core,
+  captured by wrapping ``BiAttn.left_v2._apply_rope`` (the wrapper only
+  records; the reference code computes every value),
+* the attended output (input of ``out``) and the gradients of every one of
+  the above for a seeded upstream gradient,
+* the source schedule ``topology_offsets(l, topology)`` for layers 1..24.
+
+The output is ``tests/golden/sbda_golden.npz`` (float32, a few hundred KB).
+The fixture never travels with a need for the reference: the GPU tests and
+the oracle tests only read the ``.npz``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+# (name, batch, length, dim, heads, layer) -- shapes chosen to cover the
+# reference's own test lengths (1, 7, 129; tests/test_model.py:49), the
+# config-1 smoke shape (dim 16, 2 heads, seq 32, layers 1..3), a dyadic
+# offset beyond the sequence, a merged near/far window and ragged lengths.
+CASES = [
+    ("cfg1_l1", 1, 32, 16, 2, 1),
+    ("cfg1_l2", 1, 32, 16, 2, 2),
+    ("cfg1_l3", 1, 32, 16, 2, 3),
+    ("len1_l3", 1, 1, 32, 4, 3),
+    ("len7_l11", 1, 7, 32, 4, 11),
+    ("len129_l3", 1, 129, 80, 2, 3),
+    ("b2_len17_l4", 2, 17, 32, 2, 4),
+    ("b2_len150_l8", 2, 150, 32, 2, 8),
+    ("len160_l7_d64", 1, 160, 64, 1, 7),
+]
+
+TOPOLOGIES = ("sbda", "h8", "h8a", "h8b", "h8c", "h8d", "h8e", "binary", "h0", "h1",
+              "h7", "local_jump", "longformer_local")
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", required=True)
+    parser.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "sbda_golden.npz"))
+    args = parser.parse_args()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    from BiAttn import left_v2  # noqa: E402  (reference code)
+    from BiAttn.topology import topology_offsets  # noqa: E402
+
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    arrays: dict[str, np.ndarray] = {}
+    manifest = []
+    captured: dict[str, torch.Tensor] = {}
+    original_rope = left_v2._apply_rope
+
+    def recording_rope(q, k, **kwargs):
+        rq, rk = original_rope(q, k, **kwargs)
+        rq.retain_grad()
+        rk.retain_grad()
+        captured["q"], captured["k"] = rq, rk
+        return rq, rk
+
+    left_v2._apply_rope = recording_rope
+    try:
+        for name, batch, length, dim, heads, layer in CASES:
+            torch.manual_seed(1234 + layer * 7 + length)
+            attn = left_v2.SBDAttention(dim, heads, layer, use_fused=False, total_layers=12)
+            with torch.no_grad():
+                attn.q_norm.weight.uniform_(0.5, 1.5)
+                attn.k_norm.weight.uniform_(0.5, 1.5)
+            hooks = []
+
+            def grab_v(_module, _inputs, output):
+                output.retain_grad()
+                captured["v"] = output
+
+            def grab_attended(_module, inputs):
+                inputs[0].retain_grad()
+                captured["attended"] = inputs[0]
+
+            hooks.append(attn.v.register_forward_hook(grab_v))
+            hooks.append(attn.out.register_forward_pre_hook(grab_attended))
+            x = torch.randn(batch, length, dim, requires_grad=True)
+            y = attn(x)
+            grad_y = torch.randn_like(y)
+            y.backward(grad_y)
+            for hook in hooks:
+                hook.remove()
+            head_dim = dim // heads
+            bhld = lambda t: t.detach().reshape(batch, length, heads, head_dim).permute(0, 2, 1, 3)  # noqa: E731
+            record = {
+                "x": x.detach(), "y": y.detach(), "grad_y": grad_y, "dx": x.grad,
+                "q": bhld(captured["q"]), "k": bhld(captured["k"]), "v": bhld(captured["v"]),
+                "o": bhld(captured["attended"]),
+                "do": bhld(captured["attended"].grad),
+                "dq": bhld(captured["q"].grad), "dk": bhld(captured["k"].grad),
+                "dv": bhld(captured["v"].grad),
+            }
+            for key, param in attn.state_dict().items():
+                record["param." + key] = param.detach()
+            for key, param in attn.named_parameters():
+                record["grad." + key] = param.grad.detach()
+            for key, value in record.items():
+                arrays[f"{name}/{key}"] = value.contiguous().to(torch.float32).numpy()
+            offsets = list(topology_offsets(layer, topology="sbda", total_layers=12))
+            manifest.append({"name": name, "batch": batch, "length": length, "dim": dim,
+                             "heads": heads, "layer": layer, "offsets": offsets})
+    finally:
+        left_v2._apply_rope = original_rope
+
+    schedules = {}
+    for topology in TOPOLOGIES:
+        schedules[topology] = [list(topology_offsets(layer, topology=topology, total_layers=12))
+                               for layer in range(1, 25)]
+    arrays["manifest"] = np.frombuffer(json.dumps({"cases": manifest, "schedules": schedules,
+                                                   "total_layers": 12}).encode(), dtype=np.uint8)
+    np.savez_compressed(args.out, **arrays)
+    print(f"wrote {args.out}: {len(manifest)} cases, {sum(a.nbytes for a in arrays.values())} bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,96 @@
+"""C-ABI library: builds, loads, exports every declared symbol, validates arguments.
+
+No test here launches device work: each call returns from host-side argument
+validation before any CUDA call, so the suite runs without a GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import sbda_b200
+from sbda_b200 import _lib, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "sbda_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build_library()
+    return _lib.load()
+
+
+def declared_symbols() -> list[str]:
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(sbda_b200_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_symbols()
+    assert "sbda_b200_forward" in names and "sbda_b200_backward" in names
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_matches_header(lib):
+    version = int(re.search(r"#define SBDA_B200_ABI_VERSION (\d+)", open(HEADER).read()).group(1))
+    assert lib.sbda_b200_abi_version() == version
+
+
+def test_status_strings(lib):
+    for code in range(6):
+        assert _lib.status_string(code)
+    assert "dtype" in _lib.status_string(_lib.SBDA_ERR_DTYPE)
+
+
+def _call_forward(lib, *, dtype=_lib.SBDA_DTYPE_BF16, shape=(1, 2, 2, 64, 64), offsets=(0, 1, 2, 4), n=None,
+                  ptr=16):
+    t = _lib.SbdaTensor(ptr, 1 << 20, 1 << 14, 64, 1)
+    s = _lib.SbdaShape(*shape)
+    return lib.sbda_b200_forward(dtype, s, _lib.offsets_array(offsets), len(offsets) if n is None else n,
+                                 0.125, t, t, t, t, ptr, None)
+
+
+def test_forward_validation_codes(lib):
+    assert _call_forward(lib, dtype=7) == _lib.SBDA_ERR_DTYPE
+    assert _call_forward(lib, n=5) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, n=0) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, offsets=(0, 1, 1, 4)) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, offsets=(0, -1)) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, shape=(1, 2, 2, 64, 129)) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, shape=(1, 3, 2, 64, 64)) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, shape=(1, 2, 2, 64, 0)) == _lib.SBDA_ERR_INVALID
+    assert _call_forward(lib, ptr=0) == _lib.SBDA_ERR_INVALID
+    # Two offsets beyond every tile height need two far tiles: outside the envelope.
+    assert _call_forward(lib, offsets=(0, 1000, 3000)) == _lib.SBDA_ERR_UNSUPPORTED
+    # Empty problems are a successful no-op (no device work).
+    assert _call_forward(lib, shape=(0, 2, 2, 64, 64)) == _lib.SBDA_OK
+    assert _call_forward(lib, shape=(1, 2, 2, 0, 64)) == _lib.SBDA_OK
+
+
+def test_backward_validation_codes(lib):
+    t = _lib.SbdaTensor(16, 1 << 20, 1 << 14, 64, 1)
+    s = _lib.SbdaShape(1, 2, 2, 64, 64)
+    offs = _lib.offsets_array((0, 1, 2, 4))
+    assert lib.sbda_b200_backward(9, s, offs, 4, 0.1, t, t, t, t, 16, t, t, t, None) == _lib.SBDA_ERR_DTYPE
+    assert lib.sbda_b200_backward(2, s, offs, 4, 0.1, t, t, t, t, None, t, t, t, None) == _lib.SBDA_ERR_INVALID
+
+
+def test_python_errors_follow_reference_types():
+    q = torch.randn(1, 2, 8, 16)
+    with pytest.raises(RuntimeError):
+        sbda_b200.fused_sbda_key_backward(q, q, q, (0, 1))
+    assert sbda_b200.host_offsets(torch.tensor([0, 1, 2, 8], dtype=torch.int32)) == (0, 1, 2, 8)
+    assert sbda_b200.host_offsets([0, 2]) == (0, 2)
+    module = sbda_b200.SBDAttention(16, 2, 3)
+    with pytest.raises(RuntimeError):
+        module(torch.randn(1, 4, 16))
+    with pytest.raises(ValueError):
+        sbda_b200.SBDAttention(16, 2, 3, use_fused=False)
+    assert set(module.state_dict()) == {"q.weight", "k.weight", "v.weight", "out.weight",
+                                        "q_norm.weight", "k_norm.weight"}
