@@ -44,6 +44,8 @@ def parse_args():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--length", type=int, default=1 << 20)
     p.add_argument("--layers", type=int, default=20)
+    p.add_argument("--layer-list", type=str, default="",
+                   help="comma-separated subset of layers to run (profiling cases); default all")
     p.add_argument("--heads", type=int, default=4)
     p.add_argument("--head-dim", type=int, default=64)
     p.add_argument("--e2e-steps", type=int, default=2)
@@ -228,6 +230,9 @@ def run_b200(args) -> None:
     L, H, D, layers = args.length, args.heads, args.head_dim, args.layers
     dtype = torch.bfloat16
     offsets = sbda_b200.sbda_layer_offsets(layers)
+    if args.layer_list:
+        offsets = [offsets[int(x) - 1] for x in args.layer_list.split(",")]
+        layers = len(offsets)
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
 
     def blhd():
@@ -342,7 +347,7 @@ def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
     """
     import sbda_b200
 
-    L, H, D, layers = args.length, args.heads, args.head_dim, args.layers
+    L, H, D, layers = args.length, args.heads, args.head_dim, len(offsets)
     g = torch.Generator().manual_seed(99)
     host_in = [torch.randn((1, L, H, D), generator=g).to(torch.bfloat16).pin_memory() for _ in range(4)]
     host_out = [torch.empty((1, L, H, D), dtype=torch.bfloat16).pin_memory() for _ in range(3)]

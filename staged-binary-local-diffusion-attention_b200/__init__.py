@@ -13,6 +13,7 @@ from .ops import (
     fused_sbda_gqa_key_backward,
     fused_sbda_key_backward,
     host_offsets,
+    sbda_attention,
     sbda_backward,
     sbda_forward,
 )
@@ -21,7 +22,7 @@ from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_
 __all__ = [
     "PATH_TOPOLOGIES", "SBDAttention", "SBDAAttention", "device_status", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
-    "fused_sbda_key_backward", "host_offsets", "sbda_backward", "sbda_forward",
+    "fused_sbda_key_backward", "host_offsets", "sbda_attention", "sbda_backward", "sbda_forward",
     "sbda_layer_offsets", "sbda_stage", "topology_offsets",
 ]
 

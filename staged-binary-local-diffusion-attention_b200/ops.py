@@ -210,6 +210,19 @@ def fused_sbda_block_full(q: Tensor, k: Tensor, v: Tensor, offsets: Tensor | Seq
     return _apply(q, k, v, offsets, gqa=False)
 
 
+def sbda_attention(q: Tensor, k: Tensor, v: Tensor, offsets: Tensor | Sequence[int]) -> Tensor:
+    """General entry: 1..4 distinct offsets, MHA or GQA (``k``/``v`` with fewer heads).
+
+    The reference's fused functions accept only S in (2, 4)
+    (``sbda_triton.py:1300-1301``); this one serves every schedule of
+    ``BiAttn/topology.py`` with at most four sources and at most one source
+    beyond the kernel's near window.
+    """
+    values = host_offsets(offsets)
+    _check_inputs(q, k, v, values, gqa=k.shape[1] != q.shape[1], source_counts=(1, 2, 3, 4))
+    return _SBDAFunction.apply(q, k, v, values)
+
+
 def device_status(reset: bool = True) -> int:
     """Device fault word set by the kernels instead of trapping (0 = clean)."""
     return _lib.device_status(reset)
@@ -217,5 +230,6 @@ def device_status(reset: bool = True) -> int:
 
 __all__ = [
     "fused_sbda", "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_key_backward",
-    "fused_sbda_gqa_key_backward", "sbda_forward", "sbda_backward", "host_offsets", "device_status",
+    "fused_sbda_gqa_key_backward", "sbda_attention", "sbda_forward", "sbda_backward", "host_offsets",
+    "device_status",
 ]
