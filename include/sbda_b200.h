@@ -110,6 +110,14 @@ int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int3
                        void* stream);
 
 /*
+ * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
+ * (the windowed chain-walking kernels wherever they apply, else the general
+ * ones), 1 = general kernels only.  Returns the previous setting, or -1 for
+ * an unknown value.  Both families compute the same function.
+ */
+int sbda_b200_set_kernel_path(int path);
+
+/*
  * Reads (and, if reset != 0, clears) the calling device's fault word that
  * kernels set instead of trapping (bit 0: a bounded wait on a tensor-copy
  * barrier expired).  Synchronous: waits for the device.  Not for hot paths.

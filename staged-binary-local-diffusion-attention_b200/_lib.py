@@ -87,6 +87,8 @@ def load() -> ctypes.CDLL:
             SbdaTensor, SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
+        lib.sbda_b200_set_kernel_path.restype = c_int
+        lib.sbda_b200_set_kernel_path.argtypes = [c_int]
         lib.sbda_b200_device_status.restype = c_int
         lib.sbda_b200_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_int]
         _lib = lib
@@ -114,6 +116,14 @@ def offsets_array(offsets: tuple[int, ...]):
     for index, offset in enumerate(offsets[:4]):
         array[index] = int(offset)
     return array
+
+
+def set_kernel_path(path: int) -> int:
+    """0 = automatic, 1 = general kernels only (process-wide); returns the previous value."""
+    previous = load().sbda_b200_set_kernel_path(int(path))
+    if previous < 0:
+        raise ValueError(f"unknown kernel path {path}")
+    return previous
 
 
 def device_status(reset: bool = True) -> int:

@@ -1,0 +1,510 @@
+// sbda_api.cu -- host side of the C ABI (include/sbda_b200.h): argument
+// validation, tile planning, tensor-map encoding and kernel selection.
+
+#include "sbda_common.cuh"
+
+#include <atomic>
+#include <mutex>
+#include <string.h>
+
+namespace sbda {
+
+__device__ unsigned int g_device_status = 0;
+
+// Device address of g_device_status per device (kernels receive it as a
+// pointer so every translation unit reports into one word).
+unsigned* status_ptr() {
+  static std::atomic<unsigned*> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
+  if (dev < 64) {
+    unsigned* p = cache[dev].load(std::memory_order_acquire);
+    if (p) return p;
+  }
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_device_status) != cudaSuccess) return nullptr;
+  if (dev < 64) cache[dev].store(static_cast<unsigned*>(addr), std::memory_order_release);
+  return static_cast<unsigned*>(addr);
+}
+
+std::atomic<int> g_kernel_path{0};  // 0 = automatic, 1 = general kernels only
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// --------------------------------------------------------------------------
+// Host side
+// --------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+int elem_size(int dtype) { return dtype == SBDA_DTYPE_F32 ? 4 : 2; }
+
+CUtensorMapDataType map_dtype(int dtype) {
+  return dtype == SBDA_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+         : dtype == SBDA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// Row pitch of a staged tile: D padded to a power of two, at least 128 bytes.
+int row_pitch(int64_t D, int e) {
+  int p = 128;
+  while (p < D * e) p *= 2;
+  return p;
+}
+
+struct View {
+  const void* ptr;
+  int64_t heads;
+  sbda_tensor t;
+};
+
+// A view can be staged by the copy engine / written with 16-byte vectors when
+// its base and the byte strides of every non-trivial outer dimension are
+// multiples of 16 and channels are contiguous.
+bool vector_ok(const sbda_tensor& t, int64_t B, int64_t H, int64_t L, int64_t D, int e) {
+  if (reinterpret_cast<uintptr_t>(t.data) % 16) return false;
+  if (D > 1 && t.stride_d != 1) return false;
+  if ((D * e) % 16) return false;
+  const int64_t sizes[3] = {B, H, L};
+  const int64_t strides[3] = {t.stride_b, t.stride_h, t.stride_l};
+  for (int i = 0; i < 3; ++i)
+    if (sizes[i] > 1 && (strides[i] <= 0 || (strides[i] * e) % 16)) return false;
+  return true;
+}
+
+// Encodes the (D, outer...) 4-D map of a view with a box of `rows` positions.
+// Outer dimensions are ordered by increasing stride; `slots` records where
+// position / head / batch land (2 bits each).
+bool encode_map(CUtensorMap* map, unsigned* slots, const sbda_tensor& t, int dtype, int64_t B, int64_t H,
+                int64_t L, int64_t D, int pitch, int rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const int e = elem_size(dtype);
+  int64_t size[3] = {L, H, B};
+  int64_t stride[3] = {t.stride_l * e, t.stride_h * e, t.stride_b * e};
+  int64_t big = 16;
+  for (int i = 0; i < 3; ++i)
+    if (size[i] > 1) big = (stride[i] * size[i] > big) ? stride[i] * size[i] : big;
+  for (int i = 0; i < 3; ++i)
+    if (size[i] <= 1) stride[i] = ((big + 15) / 16) * 16;  // trivial dims go outermost
+  int order[3] = {0, 1, 2};
+  for (int a = 0; a < 3; ++a)
+    for (int c = a + 1; c < 3; ++c)
+      if (stride[order[c]] < stride[order[a]]) {
+        const int tmp = order[a];
+        order[a] = order[c];
+        order[c] = tmp;
+      }
+  cuuint64_t gdim[4] = {(cuuint64_t)D, 0, 0, 0};
+  cuuint64_t gstride[3];
+  cuuint32_t box[4] = {(cuuint32_t)(pitch / e), 1, 1, 1};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  unsigned s = 0;
+  for (int k = 0; k < 3; ++k) {
+    const int d = order[k];
+    gdim[k + 1] = (cuuint64_t)size[d];
+    gstride[k] = (cuuint64_t)stride[d];
+    if (d == 0) {
+      box[k + 1] = (cuuint32_t)rows;
+      s |= (unsigned)(k + 1);
+    } else if (d == 1) {
+      s |= (unsigned)(k + 1) << 2;
+    } else {
+      s |= (unsigned)(k + 1) << 4;
+    }
+  }
+  *slots = s;
+  const CUresult r = enc(map, map_dtype(dtype), 4, const_cast<void*>(t.data), gdim, gstride, box, estride,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Splits offsets into the near window and at most one far offset for a tile
+// height, and sizes the staged regions.  Returns false when the offsets need
+// two far tiles at this tile height.
+bool plan_for_tile(const int32_t* off, int n, int64_t L, int tile, int pitch, Plan* pl) {
+  Geometry g;
+  memset(&g, 0, sizeof(g));
+  g.S = n;
+  int nfar = 0;
+  for (int s = 0; s < n; ++s) {
+    g.off[s] = off[s];
+    if (off[s] > tile) {
+      g.is_far[s] = 1;
+      g.f = off[s];
+      ++nfar;
+    } else if (off[s] > g.Hn) {
+      g.Hn = off[s];
+    }
+  }
+  if (nfar > 1) return false;
+  g.has_far = nfar;
+  g.nT = (int)((L + tile - 1) / tile);
+  g.R = g.A = g.rem = 0;
+  if (g.has_far && g.f % tile == 0) {
+    const int R = g.f / tile;
+    if (R < g.nT) {
+      g.R = R;
+      g.A = (g.nT + R - 1) / R;
+      g.rem = g.nT - (g.A - 1) * R;
+    }
+  }
+  const size_t P = pitch;
+  const size_t T = tile, Hn = g.Hn, F = g.has_far;
+  pl->tile = tile;
+  pl->pitch = pitch;
+  pl->nv = pitch / 128;
+  pl->g = g;
+  pl->smem_fwd = (T + 2 * (Hn + T) + 2 * T * F) * P + 16;
+  const size_t nc = T + Hn + F * T;
+  pl->smem_bwd = (2 * (T + Hn) + 2 * (T + 2 * Hn) + F * (2 * (T + Hn) + 2 * T + 2 * (Hn + T))) * P +
+                 nc * 4 * sizeof(float2) + 16;
+  return true;
+}
+
+constexpr size_t kMaxSmem = 227 * 1024;
+
+int make_plan(const int32_t* off, int n, int64_t L, int64_t D, int e, Plan* pl) {
+  const int pitch = row_pitch(D, e);
+  const int nv = pitch / 128;
+  const int elems = nv * (16 / e);  // floats per lane per row
+  // Tile heights instantiated per pitch, largest first.  The backward keeps
+  // TILE/16 * EPL * 2 fp32 key accumulators per thread; keep that <= 64.
+  int tiles[2] = {64, 0};
+  if (nv == 2) {
+    tiles[0] = elems <= 8 ? 64 : 32;
+    tiles[1] = elems <= 8 ? 32 : 0;
+  } else if (nv == 4) {
+    tiles[0] = 32;
+    tiles[1] = 16;
+  }
+  for (int i = 0; i < 2 && tiles[i]; ++i) {
+    Plan cand;
+    if (!plan_for_tile(off, n, L, tiles[i], pitch, &cand)) continue;
+    if (cand.smem_fwd > kMaxSmem || cand.smem_bwd > kMaxSmem) continue;
+    *pl = cand;
+    return SBDA_OK;
+  }
+  return SBDA_ERR_UNSUPPORTED;
+}
+
+
+// Plan of the windowed kernels (sbda_v2.cu).  They serve MHA schedules whose
+// near offsets lie in {0, 1, 2} with at most one far offset d > 2; the
+// backward walks chains when d is a multiple of the tile height.
+bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, int64_t B, int64_t H,
+             V2Plan* pl) {
+  if (G != 1) return false;
+  const int pitch = row_pitch(D, e);
+  const int lane_bytes = e == 4 ? 32 : 16;
+  const int lpr = pitch / lane_bytes;
+  if (lpr != 4 && lpr != 8 && lpr != 16) return false;
+  const int T = v2_tile(lpr);
+  V2Geometry g;
+  memset(&g, 0, sizeof(g));
+  int nfar = 0;
+  for (int s = 0; s < n; ++s) {
+    if (off[s] == 0) g.has0 = 1;
+    else if (off[s] == 1) g.has1 = 1;
+    else if (off[s] == 2) g.has2 = 1;
+    else if (off[s] < L) {
+      g.d = off[s];
+      ++nfar;
+    }
+    // a far offset >= L never has a valid source: it drops out of every row
+  }
+  if (nfar > 1) return false;
+  g.has_far = nfar;
+  g.nT = (int)((L + T - 1) / T);
+  if (g.has_far && g.d % T == 0 && g.d / T < g.nT) {
+    g.R = g.d / T;
+    g.A = (g.nT + g.R - 1) / g.R;
+    g.rem = g.nT - (g.A - 1) * g.R;
+  }
+  if (g.has_far && g.d >= T) {
+    if (g.d % T) return false;
+    g.mode = 0;
+    g.halo = 2;
+  } else {
+    g.mode = 1;
+    g.halo = g.has_far ? (g.d > 2 ? g.d : 2) : 2;
+  }
+  const size_t P = pitch, Tz = T, hz = g.halo;
+  pl->lpr = lpr;
+  pl->tile = T;
+  pl->pitch = pitch;
+  pl->smem_fwd = (Tz + 2 * (Tz + 2) + 2 * Tz * g.has_far) * P + 16;
+  const size_t nkv = g.mode == 0 ? 3 : 2, kvr = Tz + 2 * hz, qdr = Tz + hz;
+  pl->smem_bwd = nkv * 2 * kvr * P + 2 * 2 * qdr * P + qdr * 4 * sizeof(float2) + 16;
+  if (pl->smem_fwd > kMaxSmem || pl->smem_bwd > kMaxSmem) return false;
+  // Backward work split: about four CTAs' worth of tiles per resident slot.
+  const int64_t total = B * H * (int64_t)g.nT;
+  const int64_t target = (int64_t)sm_count() * 2 * 4;
+  int seg = (int)((total + target - 1) / target);
+  if (seg < 1) seg = 1;
+  if (g.mode == 0) {
+    if (seg < 4) seg = 4;  // amortise the carry-only first tile of a segment
+    if (seg >= g.A) seg = g.A;
+    g.seg = seg;
+    g.segs = (g.A + seg - 1) / seg;
+    pl->blocks_bwd = (unsigned)(B * H * (int64_t)g.R * g.segs);
+  } else {
+    g.seg = seg;
+    g.segs = (g.nT + seg - 1) / seg;
+    pl->blocks_bwd = (unsigned)(B * H * (int64_t)g.segs);
+  }
+  pl->g = g;
+  return true;
+}
+
+int validate(int dtype, const sbda_shape& s, const int32_t* off, int n) {
+  if (dtype != SBDA_DTYPE_F32 && dtype != SBDA_DTYPE_F16 && dtype != SBDA_DTYPE_BF16) return SBDA_ERR_DTYPE;
+  if (s.batch < 0 || s.heads < 0 || s.kv_heads < 0 || s.length < 0 || s.head_dim < 1) return SBDA_ERR_INVALID;
+  if (s.head_dim > 128) return SBDA_ERR_INVALID;
+  if (s.kv_heads == 0 ? s.heads != 0 : s.heads % s.kv_heads) return SBDA_ERR_INVALID;
+  if (s.length > (int64_t)1 << 30 || s.batch * s.heads > ((int64_t)1 << 31) / 2) return SBDA_ERR_UNSUPPORTED;
+  if (!off || n < 1 || n > 4) return SBDA_ERR_INVALID;
+  for (int a = 0; a < n; ++a) {
+    if (off[a] < 0) return SBDA_ERR_INVALID;
+    for (int c = a + 1; c < n; ++c)
+      if (off[a] == off[c]) return SBDA_ERR_INVALID;
+  }
+  return SBDA_OK;
+}
+
+TensorArg arg_of(const sbda_tensor& t) {
+  return TensorArg{t.data, t.stride_b, t.stride_h, t.stride_l, t.stride_d};
+}
+
+
+// Shape/stride eligibility shared by forward and backward.
+bool tensors_vector_ok(std::initializer_list<const sbda_tensor*> ts, int64_t B, int64_t L, int64_t D, int e,
+                       std::initializer_list<int64_t> heads) {
+  auto h = heads.begin();
+  for (const sbda_tensor* t : ts) {
+    if (!vector_ok(*t, B, *h, L, D, e)) return false;
+    ++h;
+  }
+  return true;
+}
+
+}  // namespace sbda
+
+using namespace sbda;
+
+extern "C" int sbda_b200_abi_version(void) { return SBDA_B200_ABI_VERSION; }
+
+extern "C" const char* sbda_b200_status_string(int status) {
+  switch (status) {
+    case SBDA_OK: return "ok";
+    case SBDA_ERR_INVALID: return "invalid argument (shape, stride, offsets or pointer)";
+    case SBDA_ERR_DTYPE: return "unsupported SBDA dtype";
+    case SBDA_ERR_UNSUPPORTED: return "offsets or shape outside the kernel envelope";
+    case SBDA_ERR_CUDA: return "CUDA runtime error";
+    case SBDA_ERR_DEVICE: return "device-side fault reported by an SBDA kernel";
+    default: return "unknown SBDA status";
+  }
+}
+
+extern "C" int sbda_b200_set_kernel_path(int path) {
+  if (path != 0 && path != 1) return -1;
+  return g_kernel_path.exchange(path);
+}
+
+extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                 float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v, sbda_tensor out,
+                                 float* lse, void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || L == 0) return SBDA_OK;
+  if (!q.data || !k.data || !v.data || !out.data || !lse) return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = tensors_vector_ok({&q, &k, &v, &out}, B, L, D, e, {H, Hkv, Hkv, H});
+
+  V2Plan p2;
+  if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
+    FwdV2Params p;
+    memset(&p, 0, sizeof(p));
+    p.B = (int)B;
+    p.H = (int)H;
+    p.L = (int)L;
+    p.D = (int)D;
+    p.scale = scale;
+    p.g = p2.g;
+    p.q = arg_of(q);
+    p.k = arg_of(k);
+    p.v = arg_of(v);
+    p.out = arg_of(out);
+    p.lse = lse;
+    p.status = status_ptr();
+    FwdMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    bool tma = vec;
+    if (tma) {
+      unsigned dummy;
+      tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.kT, &p.slots_k, k, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, 2) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, 2);
+    }
+    return v2_forward(dtype, tma, maps, p, p2, s);
+  }
+
+  Plan pl;
+  st = make_plan(offsets, n_offsets, L, D, e, &pl);
+  if (st != SBDA_OK) return st;
+  FwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = (int)B;
+  p.H = (int)H;
+  p.Hkv = (int)Hkv;
+  p.G = (int)(H / Hkv);
+  p.L = (int)L;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = pl.g;
+  p.q = arg_of(q);
+  p.k = arg_of(k);
+  p.v = arg_of(v);
+  p.out = arg_of(out);
+  p.lse = lse;
+  p.status = status_ptr();
+  FwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  bool tma = vec;
+  if (tma) {
+    unsigned dummy;
+    tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, pl.pitch, pl.tile) &&
+          encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, pl.pitch, pl.tile) &&
+          encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, pl.pitch, pl.tile);
+    if (tma && pl.g.Hn > 0)
+      tma = encode_map(&maps.kH, &dummy, k, dtype, B, Hkv, L, D, pl.pitch, pl.g.Hn) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, Hkv, L, D, pl.pitch, pl.g.Hn);
+  }
+  return v1_forward(dtype, tma, maps, p, pl, s);
+}
+
+extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                  float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                  sbda_tensor grad_out, const float* lse, sbda_tensor grad_q,
+                                  sbda_tensor grad_k, sbda_tensor grad_v, void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || L == 0) return SBDA_OK;
+  if (!q.data || !k.data || !v.data || !grad_out.data || !lse || !grad_q.data || !grad_k.data ||
+      !grad_v.data)
+    return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = tensors_vector_ok({&q, &k, &v, &grad_out, &grad_q, &grad_k, &grad_v}, B, L, D, e,
+                                     {H, Hkv, Hkv, H, H, Hkv, Hkv});
+
+  V2Plan p2;
+  if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
+    BwdV2Params p;
+    memset(&p, 0, sizeof(p));
+    p.B = (int)B;
+    p.H = (int)H;
+    p.L = (int)L;
+    p.D = (int)D;
+    p.scale = scale;
+    p.g = p2.g;
+    p.q = arg_of(q);
+    p.k = arg_of(k);
+    p.v = arg_of(v);
+    p.dout = arg_of(grad_out);
+    p.dq = arg_of(grad_q);
+    p.dk = arg_of(grad_k);
+    p.dv = arg_of(grad_v);
+    p.lse = lse;
+    p.status = status_ptr();
+    BwdMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    bool tma = vec;
+    if (tma) {
+      unsigned dummy;
+      const int hz = p2.g.halo;
+      tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.kT, &p.slots_k, k, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.qH, &dummy, q, dtype, B, H, L, D, p2.pitch, hz) &&
+            encode_map(&maps.dH, &dummy, grad_out, dtype, B, H, L, D, p2.pitch, hz) &&
+            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, hz) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, hz);
+    }
+    return v2_backward(dtype, tma, maps, p, p2, s);
+  }
+
+  Plan pl;
+  st = make_plan(offsets, n_offsets, L, D, e, &pl);
+  if (st != SBDA_OK) return st;
+  BwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = (int)B;
+  p.H = (int)H;
+  p.Hkv = (int)Hkv;
+  p.G = (int)(H / Hkv);
+  p.L = (int)L;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = pl.g;
+  p.q = arg_of(q);
+  p.k = arg_of(k);
+  p.v = arg_of(v);
+  p.dout = arg_of(grad_out);
+  p.dq = arg_of(grad_q);
+  p.dk = arg_of(grad_k);
+  p.dv = arg_of(grad_v);
+  p.lse = lse;
+  p.status = status_ptr();
+  BwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  bool tma = vec;
+  if (tma) {
+    unsigned dummy;
+    tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, pl.pitch, pl.tile) &&
+          encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, pl.pitch, pl.tile) &&
+          encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, pl.pitch, pl.tile) &&
+          encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, pl.pitch, pl.tile);
+    if (tma && pl.g.Hn > 0)
+      tma = encode_map(&maps.qH, &dummy, q, dtype, B, H, L, D, pl.pitch, pl.g.Hn) &&
+            encode_map(&maps.dH, &dummy, grad_out, dtype, B, H, L, D, pl.pitch, pl.g.Hn) &&
+            encode_map(&maps.kH, &dummy, k, dtype, B, Hkv, L, D, pl.pitch, pl.g.Hn) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, Hkv, L, D, pl.pitch, pl.g.Hn);
+  }
+  return v1_backward(dtype, tma, maps, p, pl, s);
+}
+
+extern "C" int sbda_b200_device_status(uint32_t* flags_out, int reset) {
+  unsigned value = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return SBDA_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&value, g_device_status, sizeof(value)) != cudaSuccess) return SBDA_ERR_CUDA;
+  if (reset) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)) != cudaSuccess) return SBDA_ERR_CUDA;
+  }
+  if (flags_out) *flags_out = value;
+  return value ? SBDA_ERR_DEVICE : SBDA_OK;
+}

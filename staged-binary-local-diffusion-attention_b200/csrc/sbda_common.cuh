@@ -1,0 +1,499 @@
+// sbda_common.cuh -- shared device helpers and launch structures of the SBDA
+// sm_100a kernels (mbarrier / TMA inline PTX, element packing, row staging).
+#pragma once
+
+#include "sbda_b200.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <math.h>
+#include <stdint.h>
+
+namespace sbda {
+
+constexpr int kThreads = 128;             // 4 warps
+constexpr int kGroups = kThreads / 8;     // 8-lane row groups per CTA
+constexpr unsigned kFaultWaitExpired = 1u;
+
+// --------------------------------------------------------------------------
+// Kernel parameters
+// --------------------------------------------------------------------------
+
+struct TensorArg {
+  const void* ptr;
+  long long sb, sh, sl, sd;  // element strides
+};
+
+struct Geometry {
+  int S;           // number of sources (1..4)
+  int off[4];      // offsets
+  int is_far[4];   // 1 for the far source
+  int Hn;          // near halo rows = largest near offset
+  int f;           // far offset (0 if none)
+  int has_far;
+  int nT;          // tiles per (batch, head)
+  int R, A, rem;   // chain order: R = f / TILE tiles per chain step (0 = linear)
+};
+
+struct FwdParams {
+  int B, H, Hkv, G, L, D;
+  float scale;
+  Geometry g;
+  TensorArg q, k, v, out;
+  float* lse;
+  unsigned slots_q, slots_k, slots_v;
+  unsigned* status;
+};
+
+struct BwdParams {
+  int B, H, Hkv, G, L, D;
+  float scale;
+  Geometry g;
+  TensorArg q, k, v, dout, dq, dk, dv;
+  const float* lse;
+  unsigned slots_q, slots_k, slots_v, slots_d;
+  unsigned* status;
+};
+
+// Tensor maps: *T = TILE-row box, *H = Hn-row halo box.
+struct FwdMaps {
+  CUtensorMap qT, kT, vT, kH, vH;
+};
+struct BwdMaps {
+  CUtensorMap qT, qH, dT, dH, kT, kH, vT, vH;
+};
+
+// --------------------------------------------------------------------------
+// Device helpers: mbarrier + TMA (inline PTX), element packing
+// --------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the barrier phase with a 2 s bound.  Returns false on expiry.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - start > 2000000000ull) return false;
+  }
+}
+
+// Records a device fault, waits once more (bounded) for copies still in
+// flight into this CTA's shared memory, and lets the caller return.
+__device__ __forceinline__ void fault_and_drain(unsigned* status, uint64_t* bar, uint32_t parity) {
+  if (threadIdx.x == 0 && status) atomicOr(status, kFaultWaitExpired);
+  (void)mbar_wait_bounded(bar, parity);
+}
+
+// 4-D tiled TMA load; coordinate 0 is the channel (always 0, so the 16-byte
+// rule on the innermost coordinate holds), slots say where position / head /
+// batch sit among coordinates 1..3 of this tensor's map.
+__device__ __forceinline__ void tma_rows(void* dst, const CUtensorMap* map, uint64_t* bar, unsigned slots,
+                                         int pos, int head, int batch) {
+  const int sl = slots & 3, sh = (slots >> 2) & 3;
+  const int c1 = sl == 1 ? pos : (sh == 1 ? head : batch);
+  const int c2 = sl == 2 ? pos : (sh == 2 ? head : batch);
+  const int c3 = sl == 3 ? pos : (sh == 3 ? head : batch);
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+template <typename TE>
+struct Elem;
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ void unpack(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+  static __device__ __forceinline__ uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+  static __device__ __forceinline__ float to_float(float x) { return x; }
+  static __device__ __forceinline__ float from_float(float x) { return x; }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ void unpack2(uint32_t w, float* f) {
+    f[0] = __uint_as_float(w << 16);
+    f[1] = __uint_as_float(w & 0xffff0000u);
+  }
+  static __device__ __forceinline__ void unpack(const uint4& u, float* f) {
+    unpack2(u.x, f);
+    unpack2(u.y, f + 2);
+    unpack2(u.z, f + 4);
+    unpack2(u.w, f + 6);
+  }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint4 pack(const float* f) {
+    return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+  }
+  static __device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
+};
+template <>
+struct Elem<__half> {
+  static __device__ __forceinline__ void unpack2(uint32_t w, float* f) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    f[0] = t.x;
+    f[1] = t.y;
+  }
+  static __device__ __forceinline__ void unpack(const uint4& u, float* f) {
+    unpack2(u.x, f);
+    unpack2(u.y, f + 2);
+    unpack2(u.z, f + 4);
+    unpack2(u.w, f + 6);
+  }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint4 pack(const float* f) {
+    return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+  }
+  static __device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_float(float x) { return __float2half_rn(x); }
+};
+
+// Row of a staged tile -> this lane's EPL floats.  Lane l8 of the row group
+// owns 16-byte vectors l8, l8+8, l8+16, ...
+template <typename TE, int NV>
+__device__ __forceinline__ void load_row(const uint8_t* row, int l8, float* f) {
+  constexpr int VE = 16 / sizeof(TE);
+#pragma unroll
+  for (int n = 0; n < NV; ++n) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + (l8 + 8 * n) * 16);
+    Elem<TE>::unpack(u, f + n * VE);
+  }
+}
+
+template <typename TE, int NV, bool VEC>
+__device__ __forceinline__ void store_row(TE* dst, long long sd, int D, int l8, const float* f) {
+  constexpr int VE = 16 / sizeof(TE);
+#pragma unroll
+  for (int n = 0; n < NV; ++n) {
+    const int c0 = (l8 + 8 * n) * VE;
+    if (c0 >= D) continue;
+    if constexpr (VEC) {
+      *reinterpret_cast<uint4*>(dst + c0) = Elem<TE>::pack(f + n * VE);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VE; ++e)
+        if (c0 + e < D) dst[(long long)(c0 + e) * sd] = Elem<TE>::from_float(f[n * VE + e]);
+    }
+  }
+}
+
+// Cooperative zero-filling load of rows [pos0, pos0 + rows) of one
+// (batch, head) slice into a staged tile (pitch = pitch_elems elements).
+// Used when a tensor's layout does not meet the copy engine's alignment rules.
+template <typename TE>
+__device__ void generic_rows(uint8_t* dst, const TensorArg& t, int batch, int head, int pos0, int rows, int L,
+                             int D, int pitch_elems) {
+  TE* out = reinterpret_cast<TE*>(dst);
+  const TE* src = reinterpret_cast<const TE*>(t.ptr);
+  const int total = rows * pitch_elems;
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const int r = e / pitch_elems, c = e - r * pitch_elems;
+    const long long pos = (long long)pos0 + r;
+    TE val = Elem<TE>::from_float(0.f);
+    if (c < D && pos >= 0 && pos < L)
+      val = src[(long long)batch * t.sb + (long long)head * t.sh + pos * t.sl + (long long)c * t.sd];
+    out[e] = val;
+  }
+}
+
+__device__ __forceinline__ int chain_tile(int idx, const Geometry& g) {
+  if (g.R == 0) return idx;
+  const int full = g.rem * g.A;
+  int r, a;
+  if (idx < full) {
+    r = idx / g.A;
+    a = idx - r * g.A;
+  } else {
+    const int j = idx - full, a1 = g.A - 1;
+    r = g.rem + j / a1;
+    a = j - (j / a1) * a1;
+  }
+  return a * g.R + r;
+}
+
+template <int EPL>
+__device__ __forceinline__ float dot(const float* a, const float* b) {
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc = fmaf(a[e], b[e], acc);
+  return acc;
+}
+
+__device__ __forceinline__ float group_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  return x;
+}
+
+
+// --------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100 f32x2 ALU ops): one instruction per two lanes of
+// math, used for the dot products and the axpy updates of every row.
+// --------------------------------------------------------------------------
+
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Eight consecutive channels of one row held by one lane, as four pairs.
+struct Frag {
+  float2 v[4];
+};
+
+__device__ __forceinline__ Frag frag_zero() {
+  Frag f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f.v[i] = make_float2(0.f, 0.f);
+  return f;
+}
+
+template <typename TE>
+struct FragIO;
+
+// 16-bit rows: a lane owns one 16-byte vector (8 elements) at byte l*16.
+template <>
+struct FragIO<__nv_bfloat16> {
+  static constexpr int kLaneBytes = 16;
+  static __device__ __forceinline__ Frag load(const uint8_t* row, int l) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + l * 16);
+    Frag f;
+    f.v[0] = make_float2(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u));
+    f.v[1] = make_float2(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+    f.v[2] = make_float2(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u));
+    f.v[3] = make_float2(__uint_as_float(u.w << 16), __uint_as_float(u.w & 0xffff0000u));
+    return f;
+  }
+  static __device__ __forceinline__ uint4 pack(const Frag& f) {
+    return make_uint4(Elem<__nv_bfloat16>::pack2(f.v[0].x, f.v[0].y), Elem<__nv_bfloat16>::pack2(f.v[1].x, f.v[1].y),
+                      Elem<__nv_bfloat16>::pack2(f.v[2].x, f.v[2].y), Elem<__nv_bfloat16>::pack2(f.v[3].x, f.v[3].y));
+  }
+};
+
+template <>
+struct FragIO<__half> {
+  static constexpr int kLaneBytes = 16;
+  static __device__ __forceinline__ Frag load(const uint8_t* row, int l) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + l * 16);
+    Frag f;
+    f.v[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    f.v[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    f.v[2] = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+    f.v[3] = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+    return f;
+  }
+  static __device__ __forceinline__ uint4 pack(const Frag& f) {
+    return make_uint4(Elem<__half>::pack2(f.v[0].x, f.v[0].y), Elem<__half>::pack2(f.v[1].x, f.v[1].y),
+                      Elem<__half>::pack2(f.v[2].x, f.v[2].y), Elem<__half>::pack2(f.v[3].x, f.v[3].y));
+  }
+};
+
+// fp32 rows: a lane owns two 16-byte vectors (8 elements) at byte l*32.
+template <>
+struct FragIO<float> {
+  static constexpr int kLaneBytes = 32;
+  static __device__ __forceinline__ Frag load(const uint8_t* row, int l) {
+    const float4 a = *reinterpret_cast<const float4*>(row + l * 32);
+    const float4 b = *reinterpret_cast<const float4*>(row + l * 32 + 16);
+    Frag f;
+    f.v[0] = make_float2(a.x, a.y);
+    f.v[1] = make_float2(a.z, a.w);
+    f.v[2] = make_float2(b.x, b.y);
+    f.v[3] = make_float2(b.z, b.w);
+    return f;
+  }
+};
+
+__device__ __forceinline__ float frag_dot(const Frag& a, const Frag& b) {
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc = fma2(a.v[i], b.v[i], acc);
+  return acc.x + acc.y;
+}
+
+// acc += w * x
+__device__ __forceinline__ void frag_axpy(Frag& acc, float w, const Frag& x) {
+  const float2 ww = make_float2(w, w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc.v[i] = fma2(ww, x.v[i], acc.v[i]);
+}
+
+__device__ __forceinline__ void frag_scale(Frag& acc, float w) {
+  const float2 ww = make_float2(w, w);
+  const float2 z = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc.v[i] = fma2(ww, acc.v[i], z);
+}
+
+__device__ __forceinline__ void frag_add(Frag& acc, const Frag& x) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc.v[i] = add2(acc.v[i], x.v[i]);
+}
+
+// Stores a lane's 8 channels of a row (channels [8l, 8l+8) of D).
+template <typename TE, bool VEC>
+__device__ __forceinline__ void store_frag(TE* row, long long sd, int D, int l, const Frag& f) {
+  const int c0 = l * 8;
+  if (c0 >= D) return;
+  if constexpr (VEC) {
+    if constexpr (sizeof(TE) == 2) {
+      *reinterpret_cast<uint4*>(row + c0) = FragIO<TE>::pack(f);
+    } else {
+      *reinterpret_cast<float4*>(row + c0) = make_float4(f.v[0].x, f.v[0].y, f.v[1].x, f.v[1].y);
+      if (c0 + 4 < D)
+        *reinterpret_cast<float4*>(row + c0 + 4) = make_float4(f.v[2].x, f.v[2].y, f.v[3].x, f.v[3].y);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (c0 + 2 * i < D) row[(long long)(c0 + 2 * i) * sd] = Elem<TE>::from_float(f.v[i].x);
+      if (c0 + 2 * i + 1 < D) row[(long long)(c0 + 2 * i + 1) * sd] = Elem<TE>::from_float(f.v[i].y);
+    }
+  }
+}
+
+// Sum over the LPR lanes of a row group (xor butterfly within the group).
+template <int LPR>
+__device__ __forceinline__ float lane_group_sum(float x) {
+#pragma unroll
+  for (int m = LPR / 2; m >= 1; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m);
+  return x;
+}
+
+// --------------------------------------------------------------------------
+// v2 launch structures (windowed / chain-walking kernels, MHA)
+// --------------------------------------------------------------------------
+
+struct V2Geometry {
+  int has0, has1, has2;  // near sources (offsets 0, 1, 2) present
+  int has_far, d;        // far source: offset d > 2
+  int nT;                // tiles per (batch, head)
+  int R, A, rem;         // chain order of tiles (forward launch order)
+  int mode;              // backward: 0 = chain walk (d % TILE == 0, d >= TILE), 1 = local tiles
+  int halo;              // backward: consumer halo rows past the tile (2, or d in mode 1)
+  int seg;               // backward: tiles per CTA
+  int segs;              // backward: segments per chain (mode 0) or per (b, h) (mode 1)
+};
+
+struct FwdV2Params {
+  int B, H, L, D;
+  float scale;
+  V2Geometry g;
+  TensorArg q, k, v, out;
+  float* lse;
+  unsigned slots_q, slots_k, slots_v;
+  unsigned* status;
+};
+
+struct BwdV2Params {
+  int B, H, L, D;
+  float scale;
+  V2Geometry g;
+  TensorArg q, k, v, dout, dq, dk, dv;
+  const float* lse;
+  unsigned slots_q, slots_k, slots_v, slots_d;
+  unsigned* status;
+};
+
+// v2 tile height for a row pitch: each of the 128/LPR row groups owns a run of
+// four consecutive rows.
+__host__ __device__ constexpr int v2_tile(int lpr) { return 4 * (kThreads / lpr); }
+
+// Host-side launchers (defined in sbda_v1.cu / sbda_v2.cu).
+struct Plan {
+  int tile;
+  int nv;
+  int pitch;
+  Geometry g;
+  size_t smem_fwd, smem_bwd;
+};
+
+int v1_forward(int dtype, bool tma, const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st);
+int v1_backward(int dtype, bool tma, const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st);
+
+struct V2Plan {
+  int lpr;
+  int tile;
+  int pitch;
+  V2Geometry g;
+  size_t smem_fwd, smem_bwd;
+  unsigned blocks_bwd;
+};
+
+int v2_forward(int dtype, bool tma, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st);
+int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
+                cudaStream_t st);
+
+}  // namespace sbda

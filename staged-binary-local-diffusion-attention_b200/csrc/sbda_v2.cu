@@ -1,0 +1,550 @@
+// sbda_v2.cu -- windowed SBDA kernels for the MHA schedules of the SBDA
+// family: near offsets within {0, 1, 2} plus at most one far offset d > 2.
+//
+// Same function as the reference's fused op (BiAttn/sbda_triton.py:1290-1360:
+// forward O and softmax statistics, key-centric gather backward) and its eager
+// oracle (BiAttn/left_v2.py:335-405).
+//
+// What differs from the general kernels (sbda_v1.cu):
+//  * A row group of LPR lanes owns a run of four consecutive rows, so the K/V
+//    rows of offsets 1 and 2 are the rows of offsets 0 of the previous two
+//    iterations: they stay unpacked in registers (a sliding window) instead of
+//    being re-read and re-converted, and every multiply-add runs on packed
+//    fp32 pairs (fma.rn.f32x2).
+//  * The backward walks dyadic chains.  When d is a multiple of the tile
+//    height, a CTA processes tiles t, t-R, t-2R, ... (R = d / TILE) of one
+//    (batch, head): the far edge of consumer j0+r feeds key j0+r-d, which is
+//    row r of the next tile of the walk, so its dK/dV contribution is carried
+//    in the same lanes' registers to the next step.  No consumer is computed
+//    twice except one "pre" tile per CTA segment, and the K/V tile staged as
+//    this step's far sources is the next step's near sources (a ring of three
+//    K/V slots; Q/dO double-buffered), with the next step's copies in flight
+//    while this step computes.
+//  * For d < TILE ("local" mode) a tile also recomputes the d consumers past
+//    its end, which are the far consumers of its last d keys.
+
+#include "sbda_common.cuh"
+
+namespace sbda {
+
+__device__ __forceinline__ int chain_tile_v2(int idx, int R, int A, int rem) {
+  if (R == 0) return idx;
+  const int full = rem * A;
+  int r, a;
+  if (idx < full) {
+    r = idx / A;
+    a = idx - r * A;
+  } else {
+    const int j = idx - full, a1 = A - 1;
+    r = rem + j / a1;
+    a = j - (j / a1) * a1;
+  }
+  return a * R + r;
+}
+
+// Stages rows [p0, p0 + rows) of a (batch, head) slice: TMA boxes of TILE
+// and halo rows, or the cooperative zero-filling loader.
+template <typename TE, bool TMA>
+struct Stager;
+
+// --------------------------------------------------------------------------
+// Forward
+// --------------------------------------------------------------------------
+
+template <typename TE, int LPR, bool TMA>
+__global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_constant__ FwdMaps maps,
+                                                               const FwdV2Params p) {
+  constexpr int T = v2_tile(LPR);
+  constexpr int P = LPR * FragIO<TE>::kLaneBytes;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const V2Geometry& g = p.g;
+  const int tid = threadIdx.x;
+  const int grp = tid / LPR, l = tid % LPR;
+
+  int bid = blockIdx.x;
+  const int h = bid % p.H;
+  bid /= p.H;
+  const int t = chain_tile_v2(bid % g.nT, g.R, g.A, g.rem);
+  const int b = bid / g.nT;
+  const int i0 = t * T;
+  const int far = g.has_far;
+
+  uint8_t* Qs = smem;
+  uint8_t* Kn = Qs + T * P;  // positions [i0-2, i0+T)
+  uint8_t* Vn = Kn + (T + 2) * P;
+  uint8_t* Kf = Vn + (T + 2) * P;  // positions [i0-d, i0-d+T)
+  uint8_t* Vf = Kf + (far ? T * P : 0);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(Vf + (far ? T * P : 0));
+
+  if constexpr (TMA) {
+    if (tid == 0) {
+      mbar_init(bar, 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar, (uint32_t)((T * (3 + 2 * far) + 4) * P));
+      tma_rows(Qs, &maps.qT, bar, p.slots_q, i0, h, b);
+      tma_rows(Kn, &maps.kH, bar, p.slots_k, i0 - 2, h, b);
+      tma_rows(Vn, &maps.vH, bar, p.slots_v, i0 - 2, h, b);
+      tma_rows(Kn + 2 * P, &maps.kT, bar, p.slots_k, i0, h, b);
+      tma_rows(Vn + 2 * P, &maps.vT, bar, p.slots_v, i0, h, b);
+      if (far) {
+        tma_rows(Kf, &maps.kT, bar, p.slots_k, i0 - g.d, h, b);
+        tma_rows(Vf, &maps.vT, bar, p.slots_v, i0 - g.d, h, b);
+      }
+    }
+    const bool ok = mbar_wait_bounded(bar, 0);
+    if (__syncthreads_or(!ok)) {
+      fault_and_drain(p.status, bar, 0);
+      return;
+    }
+  } else {
+    constexpr int PE = P / sizeof(TE);
+    generic_rows<TE>(Qs, p.q, b, h, i0, T, p.L, p.D, PE);
+    generic_rows<TE>(Kn, p.k, b, h, i0 - 2, T + 2, p.L, p.D, PE);
+    generic_rows<TE>(Vn, p.v, b, h, i0 - 2, T + 2, p.L, p.D, PE);
+    if (far) {
+      generic_rows<TE>(Kf, p.k, b, h, i0 - g.d, T, p.L, p.D, PE);
+      generic_rows<TE>(Vf, p.v, b, h, i0 - g.d, T, p.L, p.D, PE);
+    }
+    __syncthreads();
+  }
+
+  const float scale = p.scale;
+  TE* out = reinterpret_cast<TE*>(const_cast<void*>(p.out.ptr)) + (long long)b * p.out.sb +
+            (long long)h * p.out.sh;
+  float* lse = p.lse + ((long long)b * p.H + h) * p.L;
+  const int a = grp * 4;
+  Frag k1 = FragIO<TE>::load(Kn + (a + 1) * P, l), k2 = FragIO<TE>::load(Kn + a * P, l);
+  Frag v1 = FragIO<TE>::load(Vn + (a + 1) * P, l), v2 = FragIO<TE>::load(Vn + a * P, l);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = a + i, pos = i0 + r;
+    const Frag q = FragIO<TE>::load(Qs + r * P, l);
+    const Frag k0 = FragIO<TE>::load(Kn + (r + 2) * P, l);
+    const Frag v0 = FragIO<TE>::load(Vn + (r + 2) * P, l);
+    float s0 = lane_group_sum<LPR>(frag_dot(q, k0));
+    float s1 = g.has1 ? lane_group_sum<LPR>(frag_dot(q, k1)) : 0.f;
+    float s2 = g.has2 ? lane_group_sum<LPR>(frag_dot(q, k2)) : 0.f;
+    float sf = 0.f;
+    Frag vf;
+    if (far) {
+      const Frag kf = FragIO<TE>::load(Kf + r * P, l);
+      sf = lane_group_sum<LPR>(frag_dot(q, kf));
+      vf = FragIO<TE>::load(Vf + r * P, l);
+    }
+    const bool u0 = g.has0, u1 = g.has1 && pos >= 1, u2 = g.has2 && pos >= 2, uf = far && pos >= g.d;
+    s0 = u0 ? s0 * scale : -INFINITY;
+    s1 = u1 ? s1 * scale : -INFINITY;
+    s2 = u2 ? s2 * scale : -INFINITY;
+    sf = uf ? sf * scale : -INFINITY;
+    const float m = fmaxf(fmaxf(s0, s1), fmaxf(s2, sf));
+    const bool any = m != -INFINITY;
+    const float e0 = u0 ? __expf(s0 - m) : 0.f, e1 = u1 ? __expf(s1 - m) : 0.f;
+    const float e2 = u2 ? __expf(s2 - m) : 0.f, ef = uf ? __expf(sf - m) : 0.f;
+    const float sum = (e0 + e1) + (e2 + ef);
+    const float inv = any ? 1.f / sum : 0.f;
+    Frag o = frag_zero();
+    frag_axpy(o, e0 * inv, v0);
+    if (g.has1) frag_axpy(o, e1 * inv, v1);
+    if (g.has2) frag_axpy(o, e2 * inv, v2);
+    if (far) frag_axpy(o, ef * inv, vf);
+    if (pos < p.L) {
+      store_frag<TE, TMA>(out + (long long)pos * p.out.sl, p.out.sd, p.D, l, o);
+      if (l == 0) lse[pos] = any ? m + __logf(sum) : -INFINITY;
+    }
+    k2 = k1;
+    k1 = k0;
+    v2 = v1;
+    v1 = v0;
+  }
+}
+
+// --------------------------------------------------------------------------
+// Backward
+// --------------------------------------------------------------------------
+
+// Issues the copies of one K/V slot: rows [p0, p0 + halo + T + halo).
+template <typename TE, int T, int P>
+__device__ __forceinline__ void tma_kv_slot(const BwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
+                                            uint8_t* K, uint8_t* V, int p0, int halo, int h, int b) {
+  tma_rows(K, &maps.kH, bar, p.slots_k, p0, h, b);
+  tma_rows(V, &maps.vH, bar, p.slots_v, p0, h, b);
+  tma_rows(K + halo * P, &maps.kT, bar, p.slots_k, p0 + halo, h, b);
+  tma_rows(V + halo * P, &maps.vT, bar, p.slots_v, p0 + halo, h, b);
+  tma_rows(K + (halo + T) * P, &maps.kH, bar, p.slots_k, p0 + halo + T, h, b);
+  tma_rows(V + (halo + T) * P, &maps.vH, bar, p.slots_v, p0 + halo + T, h, b);
+}
+
+template <typename TE, int T, int P>
+__device__ __forceinline__ void tma_qd_slot(const BwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
+                                            uint8_t* Q, uint8_t* Dd, int j0, int halo, int h, int b) {
+  tma_rows(Q, &maps.qT, bar, p.slots_q, j0, h, b);
+  tma_rows(Dd, &maps.dT, bar, p.slots_d, j0, h, b);
+  tma_rows(Q + T * P, &maps.qH, bar, p.slots_q, j0 + T, h, b);
+  tma_rows(Dd + T * P, &maps.dH, bar, p.slots_d, j0 + T, h, b);
+}
+
+template <typename TE, int LPR, bool TMA>
+__global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_constant__ BwdMaps maps,
+                                                               const BwdV2Params p) {
+  constexpr int T = v2_tile(LPR);
+  constexpr int P = LPR * FragIO<TE>::kLaneBytes;
+  constexpr int GROUPS = kThreads / LPR;
+  constexpr int GPW = 32 / LPR;  // row groups per warp
+  extern __shared__ __align__(128) uint8_t smem[];
+  const V2Geometry& g = p.g;
+  const int tid = threadIdx.x;
+  const int grp = tid / LPR, l = tid % LPR;
+  const int chain = g.mode == 0;
+  const int Hc = g.halo;            // consumer rows past the tile; K/V slot halo on each side
+  const int KVR = T + 2 * Hc;       // rows of a K/V slot
+  const int QDR = T + Hc;           // rows of a Q/dO slot
+  const int nkv = chain ? 3 : 2;
+  const int far = g.has_far, d = g.d;
+
+  // ---- Work assignment: a walk of tiles for this CTA. ----
+  int bid = blockIdx.x;
+  int b, h, t_first, n_steps, stride, pre;
+  if (chain) {
+    const int s = bid % g.segs;
+    bid /= g.segs;
+    const int r = bid % g.R;
+    bid /= g.R;
+    h = bid % p.H;
+    b = bid / p.H;
+    const int A_r = (g.nT - 1 - r) / g.R + 1;
+    const int a_lo = s * g.seg;
+    if (a_lo >= A_r) return;
+    const int a_hi = min(a_lo + g.seg, A_r) - 1;
+    pre = a_hi + 1 < A_r;
+    t_first = (a_hi + pre) * g.R + r;
+    n_steps = a_hi - a_lo + 1 + pre;
+    stride = g.R;
+  } else {
+    const int s = bid % g.segs;
+    bid /= g.segs;
+    h = bid % p.H;
+    b = bid / p.H;
+    const int lo = s * g.seg;
+    if (lo >= g.nT) return;
+    const int hi = min(lo + g.seg, g.nT) - 1;
+    pre = 0;
+    t_first = hi;
+    n_steps = hi - lo + 1;
+    stride = 1;
+  }
+
+  uint8_t* KVbase = smem;                                  // nkv slots of [K rows][V rows]
+  uint8_t* QDbase = KVbase + nkv * 2 * KVR * P;            // 2 slots of [Q rows][dO rows]
+  float2* E = reinterpret_cast<float2*>(QDbase + 2 * 2 * QDR * P);  // [QDR][4] (p, dS)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(E + QDR * 4);
+  auto kslot = [&](int s) { return KVbase + s * 2 * KVR * P; };
+  auto vslot = [&](int s) { return KVbase + s * 2 * KVR * P + KVR * P; };
+  auto qslot = [&](int s) { return QDbase + s * 2 * QDR * P; };
+  auto dslot = [&](int s) { return QDbase + s * 2 * QDR * P + QDR * P; };
+
+  // Copies of step i into its slots (issued by thread 0 in the TMA path).
+  auto issue = [&](int i) {
+    const int t = t_first - i * stride;
+    const int j0 = t * T;
+    uint64_t* bar = bars + (i & 1);
+    if constexpr (TMA) {
+      uint32_t rows = 2 * QDR;
+      if (chain) rows += (i == 0 ? 2 : 1) * 2 * KVR;
+      else rows += 2 * KVR;
+      mbar_arrive_expect_tx(bar, rows * P);
+      if (chain) {
+        if (i == 0) tma_kv_slot<TE, T, P>(maps, p, bar, kslot(0), vslot(0), j0 - Hc, Hc, h, b);
+        const int fs = (i + 1) % 3;
+        tma_kv_slot<TE, T, P>(maps, p, bar, kslot(fs), vslot(fs), j0 - d - Hc, Hc, h, b);
+      } else {
+        tma_kv_slot<TE, T, P>(maps, p, bar, kslot(i & 1), vslot(i & 1), j0 - Hc, Hc, h, b);
+      }
+      tma_qd_slot<TE, T, P>(maps, p, bar, qslot(i & 1), dslot(i & 1), j0, Hc, h, b);
+    } else {
+      constexpr int PE = P / sizeof(TE);
+      if (chain) {
+        if (i == 0) {
+          generic_rows<TE>(kslot(0), p.k, b, h, j0 - Hc, KVR, p.L, p.D, PE);
+          generic_rows<TE>(vslot(0), p.v, b, h, j0 - Hc, KVR, p.L, p.D, PE);
+        }
+        const int fs = (i + 1) % 3;
+        generic_rows<TE>(kslot(fs), p.k, b, h, j0 - d - Hc, KVR, p.L, p.D, PE);
+        generic_rows<TE>(vslot(fs), p.v, b, h, j0 - d - Hc, KVR, p.L, p.D, PE);
+      } else {
+        generic_rows<TE>(kslot(i & 1), p.k, b, h, j0 - Hc, KVR, p.L, p.D, PE);
+        generic_rows<TE>(vslot(i & 1), p.v, b, h, j0 - Hc, KVR, p.L, p.D, PE);
+      }
+      generic_rows<TE>(qslot(i & 1), p.q, b, h, j0, QDR, p.L, p.D, PE);
+      generic_rows<TE>(dslot(i & 1), p.dout, b, h, j0, QDR, p.L, p.D, PE);
+    }
+  };
+
+  if constexpr (TMA) {
+    if (tid == 0) {
+      mbar_init(bars, 1);
+      mbar_init(bars + 1, 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) issue(0);
+  }
+
+  const float scale = p.scale;
+  const long long bh = (long long)b * p.H + h;
+  const float* lse = p.lse + bh * p.L;
+  TE* dq = reinterpret_cast<TE*>(const_cast<void*>(p.dq.ptr)) + (long long)b * p.dq.sb + (long long)h * p.dq.sh;
+  TE* dk = reinterpret_cast<TE*>(const_cast<void*>(p.dk.ptr)) + (long long)b * p.dk.sb + (long long)h * p.dk.sh;
+  TE* dv = reinterpret_cast<TE*>(const_cast<void*>(p.dv.ptr)) + (long long)b * p.dv.sb + (long long)h * p.dv.sh;
+
+  // Far-edge dK/dV contributions carried to the next tile of a chain walk.
+  Frag carry_k[4], carry_v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) carry_k[i] = carry_v[i] = frag_zero();
+
+#pragma unroll 1
+  for (int step = 0; step < n_steps; ++step) {
+    const int t = t_first - step * stride;
+    const int j0 = t * T;
+    const bool is_pre = pre && step == 0;
+    if constexpr (TMA) {
+      if (tid == 0 && step + 1 < n_steps) issue(step + 1);
+      const bool ok = mbar_wait_bounded(bars + (step & 1), (step >> 1) & 1);
+      if (__syncthreads_or(!ok)) {
+        fault_and_drain(p.status, bars + (step & 1), (step >> 1) & 1);
+        return;
+      }
+    } else {
+      issue(step);
+      __syncthreads();
+    }
+    const int ns = chain ? step % 3 : (step & 1);
+    const uint8_t* KN = kslot(ns);
+    const uint8_t* VN = vslot(ns);
+    const uint8_t* KF = chain ? kslot((step + 1) % 3) : KN;
+    const uint8_t* VF = chain ? vslot((step + 1) % 3) : VN;
+    const int fidx = chain ? Hc : Hc - d;  // far source row of consumer c = c + fidx
+    const uint8_t* Qs = qslot(step & 1);
+    const uint8_t* Ds = dslot(step & 1);
+
+    // ---- Phase 1: softmax terms of every consumer, dQ of own queries. ----
+    auto consume = [&](int c, bool act, const Frag& k0, const Frag& v0, const Frag& k1, const Frag& v1,
+                       const Frag& k2, const Frag& v2, float lq) {
+      const int q = j0 + c;
+      const Frag qf = FragIO<TE>::load(Qs + c * P, l);
+      const Frag df = FragIO<TE>::load(Ds + c * P, l);
+      float a0 = lane_group_sum<LPR>(frag_dot(qf, k0));
+      float b0 = lane_group_sum<LPR>(frag_dot(df, v0));
+      float a1 = 0.f, b1 = 0.f, a2 = 0.f, b2 = 0.f, af = 0.f, bf = 0.f;
+      if (g.has1) {
+        a1 = lane_group_sum<LPR>(frag_dot(qf, k1));
+        b1 = lane_group_sum<LPR>(frag_dot(df, v1));
+      }
+      if (g.has2) {
+        a2 = lane_group_sum<LPR>(frag_dot(qf, k2));
+        b2 = lane_group_sum<LPR>(frag_dot(df, v2));
+      }
+      Frag kf;
+      if (far) {
+        kf = FragIO<TE>::load(KF + (c + fidx) * P, l);
+        const Frag vf = FragIO<TE>::load(VF + (c + fidx) * P, l);
+        af = lane_group_sum<LPR>(frag_dot(qf, kf));
+        bf = lane_group_sum<LPR>(frag_dot(df, vf));
+      }
+      const bool inr = q < p.L;
+      const bool u0 = g.has0 && inr, u1 = g.has1 && inr && q >= 1, u2 = g.has2 && inr && q >= 2;
+      const bool uf = far && inr && q >= d;
+      const float p0 = u0 ? __expf(fmaf(a0, scale, -lq)) : 0.f;
+      const float p1 = u1 ? __expf(fmaf(a1, scale, -lq)) : 0.f;
+      const float p2 = u2 ? __expf(fmaf(a2, scale, -lq)) : 0.f;
+      const float pf = uf ? __expf(fmaf(af, scale, -lq)) : 0.f;
+      const float delta = fmaf(p0, b0, fmaf(p1, b1, fmaf(p2, b2, pf * bf)));
+      const float d0 = p0 * (b0 - delta), d1 = p1 * (b1 - delta), d2 = p2 * (b2 - delta), dfw = pf * (bf - delta);
+      if (act && c < T && inr && !is_pre) {
+        Frag gq = frag_zero();
+        frag_axpy(gq, d0 * scale, k0);
+        if (g.has1) frag_axpy(gq, d1 * scale, k1);
+        if (g.has2) frag_axpy(gq, d2 * scale, k2);
+        if (far) frag_axpy(gq, dfw * scale, kf);
+        store_frag<TE, TMA>(dq + (long long)q * p.dq.sl, p.dq.sd, p.D, l, gq);
+      }
+      if (act && l < 4) {
+        const float pv = l == 0 ? p0 : l == 1 ? p1 : l == 2 ? p2 : pf;
+        const float sv = l == 0 ? d0 : l == 1 ? d1 : l == 2 ? d2 : dfw;
+        E[c * 4 + l] = make_float2(pv, sv);
+      }
+    };
+
+    {
+      const int a = grp * 4;
+      float lq[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) lq[i] = (j0 + a + i < p.L) ? lse[j0 + a + i] : 0.f;
+      Frag k1 = FragIO<TE>::load(KN + (a + Hc - 1) * P, l), k2 = FragIO<TE>::load(KN + (a + Hc - 2) * P, l);
+      Frag v1 = FragIO<TE>::load(VN + (a + Hc - 1) * P, l), v2 = FragIO<TE>::load(VN + (a + Hc - 2) * P, l);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = a + i;
+        const Frag k0 = FragIO<TE>::load(KN + (c + Hc) * P, l);
+        const Frag v0 = FragIO<TE>::load(VN + (c + Hc) * P, l);
+        consume(c, true, k0, v0, k1, v1, k2, v2, lq[i]);
+        k2 = k1;
+        k1 = k0;
+        v2 = v1;
+        v1 = v0;
+      }
+    }
+    // Consumers past the tile: runs of xr rows; warps with no live row skip.
+    {
+      const int xr = (Hc + GROUPS - 1) / GROUPS;
+      const int warp_first = (tid >> 5) * GPW * xr;
+      if (warp_first < Hc) {
+        const int e0 = grp * xr;
+        const int cbase = T + min(e0, Hc - 1);
+        Frag k1 = FragIO<TE>::load(KN + (cbase + Hc - 1) * P, l);
+        Frag k2 = FragIO<TE>::load(KN + (cbase + Hc - 2) * P, l);
+        Frag v1 = FragIO<TE>::load(VN + (cbase + Hc - 1) * P, l);
+        Frag v2 = FragIO<TE>::load(VN + (cbase + Hc - 2) * P, l);
+#pragma unroll 1
+        for (int i = 0; i < xr; ++i) {
+          const bool act = e0 + i < Hc;
+          const int c = act ? T + e0 + i : cbase;
+          const float lq = (act && j0 + c < p.L) ? lse[j0 + c] : 0.f;
+          const Frag k0 = FragIO<TE>::load(KN + (c + Hc) * P, l);
+          const Frag v0 = FragIO<TE>::load(VN + (c + Hc) * P, l);
+          consume(c, act, k0, v0, k1, v1, k2, v2, lq);
+          k2 = k1;
+          k1 = k0;
+          v2 = v1;
+          v1 = v0;
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---- Phase 2: dK / dV of own keys, gathered from their consumers. ----
+    {
+      const int a = grp * 4;
+      Frag q1 = FragIO<TE>::load(Qs + (a + 1) * P, l), d1 = FragIO<TE>::load(Ds + (a + 1) * P, l);
+      Frag q0 = FragIO<TE>::load(Qs + a * P, l), d0 = FragIO<TE>::load(Ds + a * P, l);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = a + i;
+        const Frag q2 = FragIO<TE>::load(Qs + (r + 2) * P, l);
+        const Frag d2 = FragIO<TE>::load(Ds + (r + 2) * P, l);
+        if (!is_pre) {
+          Frag ak = carry_k[i], av = carry_v[i];
+          if (g.has0) {
+            const float2 e = E[r * 4 + 0];
+            frag_axpy(ak, e.y, q0);
+            frag_axpy(av, e.x, d0);
+          }
+          if (g.has1) {
+            const float2 e = E[(r + 1) * 4 + 1];
+            frag_axpy(ak, e.y, q1);
+            frag_axpy(av, e.x, d1);
+          }
+          if (g.has2) {
+            const float2 e = E[(r + 2) * 4 + 2];
+            frag_axpy(ak, e.y, q2);
+            frag_axpy(av, e.x, d2);
+          }
+          if (far && !chain) {
+            const int c = r + d;
+            const float2 e = E[c * 4 + 3];
+            frag_axpy(ak, e.y, FragIO<TE>::load(Qs + c * P, l));
+            frag_axpy(av, e.x, FragIO<TE>::load(Ds + c * P, l));
+          }
+          const int j = j0 + r;
+          if (j < p.L) {
+            frag_scale(ak, scale);
+            store_frag<TE, TMA>(dk + (long long)j * p.dk.sl, p.dk.sd, p.D, l, ak);
+            store_frag<TE, TMA>(dv + (long long)j * p.dv.sl, p.dv.sd, p.D, l, av);
+          }
+        }
+        if (chain && far) {
+          const float2 e = E[r * 4 + 3];
+          carry_k[i] = frag_zero();
+          carry_v[i] = frag_zero();
+          frag_axpy(carry_k[i], e.y, q0);
+          frag_axpy(carry_v[i], e.x, d0);
+        }
+        q0 = q1;
+        d0 = d1;
+        q1 = q2;
+        d1 = d2;
+      }
+    }
+    __syncthreads();  // slots of this step are refilled two steps later
+  }
+}
+
+// --------------------------------------------------------------------------
+// Launchers
+// --------------------------------------------------------------------------
+
+template <typename TE, int LPR, bool TMA>
+int launch_fwd_v2(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  auto kern = sbda_fwd_v2_kernel<TE, LPR, TMA>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_fwd) != cudaSuccess)
+    return SBDA_ERR_CUDA;
+  const long long blocks = (long long)p.B * p.H * pl.g.nT;
+  kern<<<(unsigned)blocks, kThreads, pl.smem_fwd, st>>>(maps, p);
+  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+}
+
+template <typename TE, int LPR, bool TMA>
+int launch_bwd_v2(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  auto kern = sbda_bwd_v2_kernel<TE, LPR, TMA>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
+    return SBDA_ERR_CUDA;
+  kern<<<pl.blocks_bwd, kThreads, pl.smem_bwd, st>>>(maps, p);
+  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+}
+
+template <typename TE, bool TMA>
+int fwd_v2_lpr(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  if constexpr (sizeof(TE) == 4) {
+    if (pl.lpr == 4) return launch_fwd_v2<TE, 4, TMA>(maps, p, pl, st);
+  }
+  if (pl.lpr == 8) return launch_fwd_v2<TE, 8, TMA>(maps, p, pl, st);
+  if (pl.lpr == 16) return launch_fwd_v2<TE, 16, TMA>(maps, p, pl, st);
+  return SBDA_ERR_UNSUPPORTED;
+}
+
+template <typename TE, bool TMA>
+int bwd_v2_lpr(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  if constexpr (sizeof(TE) == 4) {
+    if (pl.lpr == 4) return launch_bwd_v2<TE, 4, TMA>(maps, p, pl, st);
+  }
+  if (pl.lpr == 8) return launch_bwd_v2<TE, 8, TMA>(maps, p, pl, st);
+  if (pl.lpr == 16) return launch_bwd_v2<TE, 16, TMA>(maps, p, pl, st);
+  return SBDA_ERR_UNSUPPORTED;
+}
+
+template <bool TMA>
+int fwd_v2_dtype(int dtype, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  if (dtype == SBDA_DTYPE_F32) return fwd_v2_lpr<float, TMA>(maps, p, pl, st);
+  if (dtype == SBDA_DTYPE_F16) return fwd_v2_lpr<__half, TMA>(maps, p, pl, st);
+  return fwd_v2_lpr<__nv_bfloat16, TMA>(maps, p, pl, st);
+}
+
+template <bool TMA>
+int bwd_v2_dtype(int dtype, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  if (dtype == SBDA_DTYPE_F32) return bwd_v2_lpr<float, TMA>(maps, p, pl, st);
+  if (dtype == SBDA_DTYPE_F16) return bwd_v2_lpr<__half, TMA>(maps, p, pl, st);
+  return bwd_v2_lpr<__nv_bfloat16, TMA>(maps, p, pl, st);
+}
+
+int v2_forward(int dtype, bool tma, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  return tma ? fwd_v2_dtype<true>(dtype, maps, p, pl, st) : fwd_v2_dtype<false>(dtype, maps, p, pl, st);
+}
+
+int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
+                cudaStream_t st) {
+  return tma ? bwd_v2_dtype<true>(dtype, maps, p, pl, st) : bwd_v2_dtype<false>(dtype, maps, p, pl, st);
+}
+
+}  // namespace sbda

@@ -42,6 +42,13 @@ def test_abi_version_matches_header(lib):
     assert lib.sbda_b200_abi_version() == version
 
 
+def test_kernel_path_switch(lib):
+    assert _lib.set_kernel_path(1) == 0
+    assert _lib.set_kernel_path(0) == 1
+    with pytest.raises(ValueError):
+        _lib.set_kernel_path(7)
+
+
 def test_status_strings(lib):
     for code in range(6):
         assert _lib.status_string(code)
@@ -67,7 +74,7 @@ def test_forward_validation_codes(lib):
     assert _call_forward(lib, shape=(1, 2, 2, 64, 0)) == _lib.SBDA_ERR_INVALID
     assert _call_forward(lib, ptr=0) == _lib.SBDA_ERR_INVALID
     # Two offsets beyond every tile height need two far tiles: outside the envelope.
-    assert _call_forward(lib, offsets=(0, 1000, 3000)) == _lib.SBDA_ERR_UNSUPPORTED
+    assert _call_forward(lib, shape=(1, 2, 2, 10000, 64), offsets=(0, 1000, 3000)) == _lib.SBDA_ERR_UNSUPPORTED
     # Empty problems are a successful no-op (no device work).
     assert _call_forward(lib, shape=(0, 2, 2, 64, 64)) == _lib.SBDA_OK
     assert _call_forward(lib, shape=(1, 2, 2, 0, 64)) == _lib.SBDA_OK

@@ -15,8 +15,17 @@ import torch
 from oracle import sbda_oracle as orc
 
 import sbda_b200
+from sbda_b200 import _lib
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=["auto", "general"])
+def kernel_path(request):
+    """Runs a test through the windowed kernels (auto) and the general ones."""
+    previous = _lib.set_kernel_path(0 if request.param == "auto" else 1)
+    yield request.param
+    _lib.set_kernel_path(previous)
 
 TOL = {torch.float32: dict(rtol=1e-5, atol=1e-5),
        torch.bfloat16: dict(rtol=0.0, atol=2e-2),
@@ -127,26 +136,26 @@ def test_reference_golden_vectors(golden):
 
 @pytest.mark.parametrize("layer", list(range(1, 13)))
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_every_layer_schedule(layer, dtype):
+def test_every_layer_schedule(layer, dtype, kernel_path):
     offsets = sbda_b200.topology_offsets(layer)
     _check(2, 2, 1000, 64, dtype, offsets, seed=layer)
 
 
-@pytest.mark.parametrize("length", [1, 2, 3, 7, 63, 64, 65, 129, 4099])
-def test_ragged_lengths(length):
+@pytest.mark.parametrize("length", [1, 2, 3, 7, 63, 64, 65, 129, 4099, 20000])
+def test_ragged_lengths(length, kernel_path):
     for layer in (1, 3, 8, 13):
         _check(1, 3, length, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), seed=length + layer)
 
 
 @pytest.mark.parametrize("dim", [8, 16, 24, 40, 64, 96, 128])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-def test_head_dims_and_dtypes(dim, dtype):
+def test_head_dims_and_dtypes(dim, dtype, kernel_path):
     for layer in (3, 9):
         _check(1, 2, 300, dim, dtype, sbda_b200.topology_offsets(layer), seed=dim)
 
 
 @pytest.mark.parametrize("layout", ["bhld", "blhd", "misaligned"])
-def test_layouts(layout):
+def test_layouts(layout, kernel_path):
     for layer in (2, 7, 10):
         _check(2, 2, 700, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), layout=layout)
     _check(1, 2, 200, 6, torch.float32, (0, 1, 2, 16), layout="bhld")  # 12-byte rows: generic path
@@ -165,18 +174,41 @@ def test_gqa_groups(kv_heads):
         _check(1, 8, 257, 32, torch.float32, sbda_b200.topology_offsets(layer), kv_heads=kv_heads)
 
 
-def test_other_offset_sets():
+def test_other_offset_sets(kernel_path):
     for offsets in ((0,), (0, 3), (0, 1, 2), (0, 1, 2, 3), (0, 5, 64), (0, 2, 100), (0, 1, 64, 200),
-                    (4, 0), (0, 1, 2, 65)):
+                    (4, 0), (0, 1, 2, 65), (2, 0, 1, 128), (0, 1, 2, 32), (0, 1, 2, 63), (0, 1, 2, 399),
+                    (0, 1, 2, 400), (0, 1, 2, 5000)):
         _check(1, 2, 400, 32, torch.float32, offsets)
 
 
-def test_offsets_without_self_source():
+@pytest.mark.parametrize("layer", [1, 2, 3, 6, 7, 8, 12, 15])
+def test_chain_walk_segments(layer, kernel_path):
+    """Long sequences split the backward's chain walks into segments with a carry-only first tile."""
+    _check(1, 4, 65536, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), seed=100 + layer)
+
+
+def test_kernel_families_agree():
+    """The windowed and the general kernels give the same results on the same inputs."""
+    q, k, v, do = _inputs(2, 4, 3000, 64, torch.bfloat16, seed=11)
+    for layer in (2, 5, 7, 9, 11):
+        offsets = sbda_b200.topology_offsets(layer)
+        previous = _lib.set_kernel_path(0)
+        try:
+            auto = _run(q, k, v, do, offsets)
+            _lib.set_kernel_path(1)
+            general = _run(q, k, v, do, offsets)
+        finally:
+            _lib.set_kernel_path(previous)
+        for a, b in zip(auto, general):
+            torch.testing.assert_close(a.float(), b.float(), rtol=0, atol=1.6e-2)
+
+
+def test_offsets_without_self_source(kernel_path):
     """Rows with no valid source give zero output and zero gradients (left_v2.py:392-393)."""
     _check(1, 2, 50, 16, torch.float32, (3, 7))
 
 
-def test_deterministic():
+def test_deterministic(kernel_path):
     q, k, v, do = _inputs(2, 4, 5000, 64, torch.bfloat16, seed=9)
     first = _run(q, k, v, do, sbda_b200.topology_offsets(9))
     second = _run(q, k, v, do, sbda_b200.topology_offsets(9))
@@ -184,7 +216,7 @@ def test_deterministic():
         assert torch.equal(a, b)
 
 
-def test_full_size_sampled_rows():
+def test_full_size_sampled_rows(kernel_path):
     """1M positions at layer 20 (dyadic 2^19): sampled rows against the fp64 row oracle."""
     length = 1 << 20
     offsets = sbda_b200.topology_offsets(20)
