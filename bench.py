@@ -293,6 +293,12 @@ def run_b200(args) -> None:
     torch.cuda.synchronize()
     fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in fwd_events)
     bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in bwd_events)
+    # per-layer launch times (forward in layer order; backward recorded in reverse)
+    n_rec = len(fwd_events) // layers
+    fwd_layer_ms = [statistics.mean(fwd_events[k * layers + j][0].elapsed_time(fwd_events[k * layers + j][1])
+                                    for k in range(n_rec)) for j in range(layers)]
+    bwd_layer_ms = [statistics.mean(bwd_events[k * layers + (layers - 1 - j)][0].elapsed_time(
+        bwd_events[k * layers + (layers - 1 - j)][1]) for k in range(n_rec)) for j in range(layers)]
 
     rows = H * L
     e = 2
@@ -328,7 +334,9 @@ def run_b200(args) -> None:
                          "launch_ms": dominant[2]},
             "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
                               "algorithmic_bytes_per_step": step_bytes, "fwd_launch_ms": fwd_ms,
-                              "bwd_launch_ms": bwd_ms},
+                              "bwd_launch_ms": bwd_ms,
+                              "fwd_layer_ms": [round(x, 4) for x in fwd_layer_ms],
+                              "bwd_layer_ms": [round(x, 4) for x in bwd_layer_ms]},
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,

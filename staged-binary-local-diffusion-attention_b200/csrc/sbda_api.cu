@@ -251,12 +251,12 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   pl->tile = T;
   pl->pitch = pitch;
   pl->smem_fwd = (Tz + 2 * (Tz + 2) + 2 * Tz * g.has_far) * P + 16;
-  const size_t nkv = g.mode == 0 ? 3 : 2, kvr = Tz + 2 * hz, qdr = Tz + hz;
+  const size_t nkv = g.mode == 0 ? 2 : 1, kvr = Tz + 2 * hz, qdr = Tz + hz;
   pl->smem_bwd = nkv * 2 * kvr * P + 2 * 2 * qdr * P + qdr * 4 * sizeof(float2) + 16;
   if (pl->smem_fwd > kMaxSmem || pl->smem_bwd > kMaxSmem) return false;
   // Backward work split: about four CTAs' worth of tiles per resident slot.
   const int64_t total = B * H * (int64_t)g.nT;
-  const int64_t target = (int64_t)sm_count() * 2 * 4;
+  const int64_t target = (int64_t)sm_count() * 3 * 4;
   int seg = (int)((total + target - 1) / target);
   if (seg < 1) seg = 1;
   if (g.mode == 0) {

@@ -288,24 +288,20 @@ __device__ __forceinline__ float group_sum(float x) {
 // math, used for the dot products and the axpy updates of every row.
 // --------------------------------------------------------------------------
 
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// 2^x on the special-function unit (ex2.approx: relative error ~2^-22).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Eight consecutive channels of one row held by one lane, as four pairs.
@@ -392,9 +388,17 @@ __device__ __forceinline__ void frag_axpy(Frag& acc, float w, const Frag& x) {
 
 __device__ __forceinline__ void frag_scale(Frag& acc, float w) {
   const float2 ww = make_float2(w, w);
-  const float2 z = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) acc.v[i] = fma2(ww, acc.v[i], z);
+  for (int i = 0; i < 4; ++i) acc.v[i] = mul2(ww, acc.v[i]);
+}
+
+// acc = w * x
+__device__ __forceinline__ Frag frag_mul(float w, const Frag& x) {
+  const float2 ww = make_float2(w, w);
+  Frag r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r.v[i] = mul2(ww, x.v[i]);
+  return r;
 }
 
 __device__ __forceinline__ void frag_add(Frag& acc, const Frag& x) {

@@ -17,9 +17,10 @@
 //    row r of the next tile of the walk, so its dK/dV contribution is carried
 //    in the same lanes' registers to the next step.  No consumer is computed
 //    twice except one "pre" tile per CTA segment, and the K/V tile staged as
-//    this step's far sources is the next step's near sources (a ring of three
-//    K/V slots; Q/dO double-buffered), with the next step's copies in flight
-//    while this step computes.
+//    this step's far sources is the next step's near sources.  Two K/V slots
+//    alternate: phase 2 (the key gather) reads no K/V, so the next step's far
+//    tile is fetched into this step's near slot as soon as phase 1 is done;
+//    Q/dO are double-buffered and fetched a whole step ahead.
 //  * For d < TILE ("local" mode) a tile also recomputes the d consumers past
 //    its end, which are the far consumers of its last d keys.
 
@@ -42,16 +43,13 @@ __device__ __forceinline__ int chain_tile_v2(int idx, int R, int A, int rem) {
   return a * R + r;
 }
 
-// Stages rows [p0, p0 + rows) of a (batch, head) slice: TMA boxes of TILE
-// and halo rows, or the cooperative zero-filling loader.
-template <typename TE, bool TMA>
-struct Stager;
-
 // --------------------------------------------------------------------------
 // Forward
 // --------------------------------------------------------------------------
 
-template <typename TE, int LPR, bool TMA>
+// Source-set shapes of the forward: 0 = flags read at run time, 1 = {0, 1},
+// 2 = {0, 2}, 3 = {0, 1, 2, d}.
+template <typename TE, int LPR, bool TMA, int SHAPE>
 __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_constant__ FwdMaps maps,
                                                                const FwdV2Params p) {
   constexpr int T = v2_tile(LPR);
@@ -67,7 +65,10 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   const int t = chain_tile_v2(bid % g.nT, g.R, g.A, g.rem);
   const int b = bid / g.nT;
   const int i0 = t * T;
-  const int far = g.has_far;
+  const bool has1 = SHAPE == 0 ? g.has1 != 0 : (SHAPE == 1 || SHAPE == 3);
+  const bool has2 = SHAPE == 0 ? g.has2 != 0 : SHAPE >= 2;
+  const bool far = SHAPE == 0 ? g.has_far != 0 : SHAPE == 3;
+  const bool has0 = SHAPE == 0 ? g.has0 != 0 : true;
 
   uint8_t* Qs = smem;
   uint8_t* Kn = Qs + T * P;  // positions [i0-2, i0+T)
@@ -111,7 +112,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
     __syncthreads();
   }
 
-  const float scale = p.scale;
+  const float c1 = p.scale * kLog2e;
   TE* out = reinterpret_cast<TE*>(const_cast<void*>(p.out.ptr)) + (long long)b * p.out.sb +
             (long long)h * p.out.sh;
   float* lse = p.lse + ((long long)b * p.H + h) * p.L;
@@ -125,8 +126,8 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
     const Frag k0 = FragIO<TE>::load(Kn + (r + 2) * P, l);
     const Frag v0 = FragIO<TE>::load(Vn + (r + 2) * P, l);
     float s0 = lane_group_sum<LPR>(frag_dot(q, k0));
-    float s1 = g.has1 ? lane_group_sum<LPR>(frag_dot(q, k1)) : 0.f;
-    float s2 = g.has2 ? lane_group_sum<LPR>(frag_dot(q, k2)) : 0.f;
+    float s1 = has1 ? lane_group_sum<LPR>(frag_dot(q, k1)) : 0.f;
+    float s2 = has2 ? lane_group_sum<LPR>(frag_dot(q, k2)) : 0.f;
     float sf = 0.f;
     Frag vf;
     if (far) {
@@ -134,25 +135,25 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
       sf = lane_group_sum<LPR>(frag_dot(q, kf));
       vf = FragIO<TE>::load(Vf + r * P, l);
     }
-    const bool u0 = g.has0, u1 = g.has1 && pos >= 1, u2 = g.has2 && pos >= 2, uf = far && pos >= g.d;
-    s0 = u0 ? s0 * scale : -INFINITY;
-    s1 = u1 ? s1 * scale : -INFINITY;
-    s2 = u2 ? s2 * scale : -INFINITY;
-    sf = uf ? sf * scale : -INFINITY;
+    // scores in log2 units: s * scale * log2(e)
+    const bool u0 = has0, u1 = has1 && pos >= 1, u2 = has2 && pos >= 2, uf = far && pos >= g.d;
+    s0 = u0 ? s0 * c1 : -INFINITY;
+    s1 = u1 ? s1 * c1 : -INFINITY;
+    s2 = u2 ? s2 * c1 : -INFINITY;
+    sf = uf ? sf * c1 : -INFINITY;
     const float m = fmaxf(fmaxf(s0, s1), fmaxf(s2, sf));
     const bool any = m != -INFINITY;
-    const float e0 = u0 ? __expf(s0 - m) : 0.f, e1 = u1 ? __expf(s1 - m) : 0.f;
-    const float e2 = u2 ? __expf(s2 - m) : 0.f, ef = uf ? __expf(sf - m) : 0.f;
+    const float e0 = u0 ? fast_exp2(s0 - m) : 0.f, e1 = u1 ? fast_exp2(s1 - m) : 0.f;
+    const float e2 = u2 ? fast_exp2(s2 - m) : 0.f, ef = uf ? fast_exp2(sf - m) : 0.f;
     const float sum = (e0 + e1) + (e2 + ef);
-    const float inv = any ? 1.f / sum : 0.f;
-    Frag o = frag_zero();
-    frag_axpy(o, e0 * inv, v0);
-    if (g.has1) frag_axpy(o, e1 * inv, v1);
-    if (g.has2) frag_axpy(o, e2 * inv, v2);
+    const float inv = any ? __frcp_rn(sum) : 0.f;
+    Frag o = frag_mul(e0 * inv, v0);
+    if (has1) frag_axpy(o, e1 * inv, v1);
+    if (has2) frag_axpy(o, e2 * inv, v2);
     if (far) frag_axpy(o, ef * inv, vf);
     if (pos < p.L) {
       store_frag<TE, TMA>(out + (long long)pos * p.out.sl, p.out.sd, p.D, l, o);
-      if (l == 0) lse[pos] = any ? m + __logf(sum) : -INFINITY;
+      if (l == 0) lse[pos] = any ? (m + __log2f(sum)) * kLn2 : -INFINITY;
     }
     k2 = k1;
     k1 = k0;
@@ -186,34 +187,55 @@ __device__ __forceinline__ void tma_qd_slot(const BwdMaps& maps, const BwdV2Para
   tma_rows(Dd + T * P, &maps.dH, bar, p.slots_d, j0 + T, h, b);
 }
 
-template <typename TE, int LPR, bool TMA>
-__global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_constant__ BwdMaps maps,
-                                                               const BwdV2Params p) {
+// Source-set shapes the backward is compiled for.  0 reads the flags at run
+// time; the others fix them so the per-row code is straight-line:
+//   1: {0, 1} (SBDA layer 1)          2: {0, 2} (SBDA layer 2)
+//   3: {0, 1, 2, d}, d < TILE (local) 4: {0, 1, 2, d}, d % TILE == 0 (chain walk)
+template <int SHAPE>
+struct BwdShape {
+  static constexpr bool kGeneric = SHAPE == 0;
+  static constexpr bool kHas1 = SHAPE == 1 || SHAPE >= 3;
+  static constexpr bool kHas2 = SHAPE >= 2;
+  static constexpr bool kFar = SHAPE >= 3;
+  static constexpr bool kChain = SHAPE == 4;
+};
+
+template <typename TE, int LPR, bool TMA, int SHAPE>
+__global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_constant__ BwdMaps maps,
+                                                                  const BwdV2Params p) {
   constexpr int T = v2_tile(LPR);
   constexpr int P = LPR * FragIO<TE>::kLaneBytes;
   constexpr int GROUPS = kThreads / LPR;
   constexpr int GPW = 32 / LPR;  // row groups per warp
+  using Sh = BwdShape<SHAPE>;
   extern __shared__ __align__(128) uint8_t smem[];
   const V2Geometry& g = p.g;
   const int tid = threadIdx.x;
   const int grp = tid / LPR, l = tid % LPR;
-  const int chain = g.mode == 0;
-  const int Hc = g.halo;            // consumer rows past the tile; K/V slot halo on each side
-  const int KVR = T + 2 * Hc;       // rows of a K/V slot
-  const int QDR = T + Hc;           // rows of a Q/dO slot
-  const int nkv = chain ? 3 : 2;
-  const int far = g.has_far, d = g.d;
+  const bool has0 = Sh::kGeneric ? g.has0 != 0 : true;
+  const bool has1 = Sh::kGeneric ? g.has1 != 0 : Sh::kHas1;
+  const bool has2 = Sh::kGeneric ? g.has2 != 0 : Sh::kHas2;
+  const bool far = Sh::kGeneric ? g.has_far != 0 : Sh::kFar;
+  const bool chain = Sh::kGeneric ? g.mode == 0 : Sh::kChain;
+  const int Hc = (Sh::kChain || SHAPE == 1 || SHAPE == 2) ? 2 : g.halo;  // consumer rows past the tile
+  const int KVR = T + 2 * Hc;  // rows of a K/V slot
+  const int QDR = T + Hc;      // rows of a Q/dO slot
+  const int nkv = chain ? 2 : 1;
+  const int d = g.d;
 
   // ---- Work assignment: a walk of tiles for this CTA. ----
+  // Heads vary fastest across consecutive CTAs: the rows of all heads of a
+  // position share DRAM pages and L2 lines in the [B, L, H, D] layout, so
+  // the heads of one walk segment run side by side.
   int bid = blockIdx.x;
   int b, h, t_first, n_steps, stride, pre;
+  h = bid % p.H;
+  bid /= p.H;
   if (chain) {
     const int s = bid % g.segs;
     bid /= g.segs;
     const int r = bid % g.R;
-    bid /= g.R;
-    h = bid % p.H;
-    b = bid / p.H;
+    b = bid / g.R;
     const int A_r = (g.nT - 1 - r) / g.R + 1;
     const int a_lo = s * g.seg;
     if (a_lo >= A_r) return;
@@ -224,9 +246,7 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
     stride = g.R;
   } else {
     const int s = bid % g.segs;
-    bid /= g.segs;
-    h = bid % p.H;
-    b = bid / p.H;
+    b = bid / g.segs;
     const int lo = s * g.seg;
     if (lo >= g.nT) return;
     const int hi = min(lo + g.seg, g.nT) - 1;
@@ -236,63 +256,70 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
     stride = 1;
   }
 
-  uint8_t* KVbase = smem;                                  // nkv slots of [K rows][V rows]
-  uint8_t* QDbase = KVbase + nkv * 2 * KVR * P;            // 2 slots of [Q rows][dO rows]
-  float2* E = reinterpret_cast<float2*>(QDbase + 2 * 2 * QDR * P);  // [QDR][4] (p, dS)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(E + QDR * 4);
+  uint8_t* KVbase = smem;                        // nkv slots of [K rows][V rows]
+  uint8_t* QDbase = KVbase + nkv * 2 * KVR * P;  // 2 slots of [Q rows][dO rows]
+  // Per consumer: (p0, ds0, p1, ds1) (p2, ds2, pf, dsf); ds already scaled by head_dim^-0.5.
+  float4* E = reinterpret_cast<float4*>(QDbase + 2 * 2 * QDR * P);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(E + QDR * 2);
   auto kslot = [&](int s) { return KVbase + s * 2 * KVR * P; };
   auto vslot = [&](int s) { return KVbase + s * 2 * KVR * P + KVR * P; };
   auto qslot = [&](int s) { return QDbase + s * 2 * QDR * P; };
   auto dslot = [&](int s) { return QDbase + s * 2 * QDR * P + QDR * P; };
 
-  // Copies of step i into its slots (issued by thread 0 in the TMA path).
-  auto issue = [&](int i) {
-    const int t = t_first - i * stride;
-    const int j0 = t * T;
-    uint64_t* bar = bars + (i & 1);
+  // Copies of step i: the Q/dO batch (issued a whole step ahead) and the K/V
+  // batch (issued once phase 1 of the previous step has released its slot).
+  // Each batch is one arrival on the step's barrier (count 2).
+  auto issue_qd = [&](int i) {
+    const int j0 = (t_first - i * stride) * T;
     if constexpr (TMA) {
-      uint32_t rows = 2 * QDR;
-      if (chain) rows += (i == 0 ? 2 : 1) * 2 * KVR;
-      else rows += 2 * KVR;
-      mbar_arrive_expect_tx(bar, rows * P);
-      if (chain) {
-        if (i == 0) tma_kv_slot<TE, T, P>(maps, p, bar, kslot(0), vslot(0), j0 - Hc, Hc, h, b);
-        const int fs = (i + 1) % 3;
-        tma_kv_slot<TE, T, P>(maps, p, bar, kslot(fs), vslot(fs), j0 - d - Hc, Hc, h, b);
-      } else {
-        tma_kv_slot<TE, T, P>(maps, p, bar, kslot(i & 1), vslot(i & 1), j0 - Hc, Hc, h, b);
-      }
+      uint64_t* bar = bars + (i & 1);
+      mbar_arrive_expect_tx(bar, (uint32_t)(2 * QDR * P));
       tma_qd_slot<TE, T, P>(maps, p, bar, qslot(i & 1), dslot(i & 1), j0, Hc, h, b);
     } else {
       constexpr int PE = P / sizeof(TE);
-      if (chain) {
-        if (i == 0) {
-          generic_rows<TE>(kslot(0), p.k, b, h, j0 - Hc, KVR, p.L, p.D, PE);
-          generic_rows<TE>(vslot(0), p.v, b, h, j0 - Hc, KVR, p.L, p.D, PE);
-        }
-        const int fs = (i + 1) % 3;
-        generic_rows<TE>(kslot(fs), p.k, b, h, j0 - d - Hc, KVR, p.L, p.D, PE);
-        generic_rows<TE>(vslot(fs), p.v, b, h, j0 - d - Hc, KVR, p.L, p.D, PE);
-      } else {
-        generic_rows<TE>(kslot(i & 1), p.k, b, h, j0 - Hc, KVR, p.L, p.D, PE);
-        generic_rows<TE>(vslot(i & 1), p.v, b, h, j0 - Hc, KVR, p.L, p.D, PE);
-      }
       generic_rows<TE>(qslot(i & 1), p.q, b, h, j0, QDR, p.L, p.D, PE);
       generic_rows<TE>(dslot(i & 1), p.dout, b, h, j0, QDR, p.L, p.D, PE);
+    }
+  };
+  auto issue_kv = [&](int i) {
+    const int j0 = (t_first - i * stride) * T;
+    // chain: step 0 stages its near slot 0 and far slot 1; step i > 0 stages
+    // only its far tile, into slot (i + 1) & 1 (its near tile is step i-1's far).
+    const int first = chain ? (i == 0 ? 0 : 1) : 0;
+    if constexpr (TMA) {
+      uint64_t* bar = bars + (i & 1);
+      mbar_arrive_expect_tx(bar, (uint32_t)((chain && i == 0 ? 2 : 1) * 2 * KVR * P));
+      for (int part = first; part < (chain ? 2 : 1); ++part) {
+        const int slot = chain ? ((i + part) & 1) : 0;
+        const int p0 = part == 0 ? j0 - Hc : j0 - d - Hc;
+        tma_kv_slot<TE, T, P>(maps, p, bar, kslot(slot), vslot(slot), p0, Hc, h, b);
+      }
+    } else {
+      constexpr int PE = P / sizeof(TE);
+      for (int part = first; part < (chain ? 2 : 1); ++part) {
+        const int slot = chain ? ((i + part) & 1) : 0;
+        const int p0 = part == 0 ? j0 - Hc : j0 - d - Hc;
+        generic_rows<TE>(kslot(slot), p.k, b, h, p0, KVR, p.L, p.D, PE);
+        generic_rows<TE>(vslot(slot), p.v, b, h, p0, KVR, p.L, p.D, PE);
+      }
     }
   };
 
   if constexpr (TMA) {
     if (tid == 0) {
-      mbar_init(bars, 1);
-      mbar_init(bars + 1, 1);
+      mbar_init(bars, 2);
+      mbar_init(bars + 1, 2);
       fence_barrier_init();
     }
     __syncthreads();
-    if (tid == 0) issue(0);
+    if (tid == 0) {
+      issue_qd(0);
+      issue_kv(0);
+    }
   }
 
   const float scale = p.scale;
+  const float c1 = scale * kLog2e;  // exp(a * scale - lse) = 2^(a * c1 - lse * log2 e)
   const long long bh = (long long)b * p.H + h;
   const float* lse = p.lse + bh * p.L;
   TE* dq = reinterpret_cast<TE*>(const_cast<void*>(p.dq.ptr)) + (long long)b * p.dq.sb + (long long)h * p.dq.sh;
@@ -310,39 +337,40 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
     const int j0 = t * T;
     const bool is_pre = pre && step == 0;
     if constexpr (TMA) {
-      if (tid == 0 && step + 1 < n_steps) issue(step + 1);
+      if (tid == 0 && step + 1 < n_steps) issue_qd(step + 1);
       const bool ok = mbar_wait_bounded(bars + (step & 1), (step >> 1) & 1);
       if (__syncthreads_or(!ok)) {
         fault_and_drain(p.status, bars + (step & 1), (step >> 1) & 1);
         return;
       }
     } else {
-      issue(step);
+      issue_qd(step);
+      issue_kv(step);
       __syncthreads();
     }
-    const int ns = chain ? step % 3 : (step & 1);
+    const int ns = chain ? (step & 1) : 0;
     const uint8_t* KN = kslot(ns);
     const uint8_t* VN = vslot(ns);
-    const uint8_t* KF = chain ? kslot((step + 1) % 3) : KN;
-    const uint8_t* VF = chain ? vslot((step + 1) % 3) : VN;
+    const uint8_t* KF = chain ? kslot(ns ^ 1) : KN;
+    const uint8_t* VF = chain ? vslot(ns ^ 1) : VN;
     const int fidx = chain ? Hc : Hc - d;  // far source row of consumer c = c + fidx
     const uint8_t* Qs = qslot(step & 1);
     const uint8_t* Ds = dslot(step & 1);
 
     // ---- Phase 1: softmax terms of every consumer, dQ of own queries. ----
     auto consume = [&](int c, bool act, const Frag& k0, const Frag& v0, const Frag& k1, const Frag& v1,
-                       const Frag& k2, const Frag& v2, float lq) {
+                       const Frag& k2, const Frag& v2, float lq2) {
       const int q = j0 + c;
       const Frag qf = FragIO<TE>::load(Qs + c * P, l);
       const Frag df = FragIO<TE>::load(Ds + c * P, l);
-      float a0 = lane_group_sum<LPR>(frag_dot(qf, k0));
-      float b0 = lane_group_sum<LPR>(frag_dot(df, v0));
+      const float a0 = lane_group_sum<LPR>(frag_dot(qf, k0));
+      const float b0 = lane_group_sum<LPR>(frag_dot(df, v0));
       float a1 = 0.f, b1 = 0.f, a2 = 0.f, b2 = 0.f, af = 0.f, bf = 0.f;
-      if (g.has1) {
+      if (has1) {
         a1 = lane_group_sum<LPR>(frag_dot(qf, k1));
         b1 = lane_group_sum<LPR>(frag_dot(df, v1));
       }
-      if (g.has2) {
+      if (has2) {
         a2 = lane_group_sum<LPR>(frag_dot(qf, k2));
         b2 = lane_group_sum<LPR>(frag_dot(df, v2));
       }
@@ -354,26 +382,25 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
         bf = lane_group_sum<LPR>(frag_dot(df, vf));
       }
       const bool inr = q < p.L;
-      const bool u0 = g.has0 && inr, u1 = g.has1 && inr && q >= 1, u2 = g.has2 && inr && q >= 2;
+      const bool u0 = has0 && inr, u1 = has1 && inr && q >= 1, u2 = has2 && inr && q >= 2;
       const bool uf = far && inr && q >= d;
-      const float p0 = u0 ? __expf(fmaf(a0, scale, -lq)) : 0.f;
-      const float p1 = u1 ? __expf(fmaf(a1, scale, -lq)) : 0.f;
-      const float p2 = u2 ? __expf(fmaf(a2, scale, -lq)) : 0.f;
-      const float pf = uf ? __expf(fmaf(af, scale, -lq)) : 0.f;
+      const float p0 = u0 ? fast_exp2(fmaf(a0, c1, -lq2)) : 0.f;
+      const float p1 = u1 ? fast_exp2(fmaf(a1, c1, -lq2)) : 0.f;
+      const float p2 = u2 ? fast_exp2(fmaf(a2, c1, -lq2)) : 0.f;
+      const float pf = uf ? fast_exp2(fmaf(af, c1, -lq2)) : 0.f;
       const float delta = fmaf(p0, b0, fmaf(p1, b1, fmaf(p2, b2, pf * bf)));
-      const float d0 = p0 * (b0 - delta), d1 = p1 * (b1 - delta), d2 = p2 * (b2 - delta), dfw = pf * (bf - delta);
+      const float d0 = p0 * (b0 - delta) * scale, d1 = p1 * (b1 - delta) * scale;
+      const float d2 = p2 * (b2 - delta) * scale, dfw = pf * (bf - delta) * scale;
       if (act && c < T && inr && !is_pre) {
-        Frag gq = frag_zero();
-        frag_axpy(gq, d0 * scale, k0);
-        if (g.has1) frag_axpy(gq, d1 * scale, k1);
-        if (g.has2) frag_axpy(gq, d2 * scale, k2);
-        if (far) frag_axpy(gq, dfw * scale, kf);
+        Frag gq = frag_mul(d0, k0);
+        if (has1) frag_axpy(gq, d1, k1);
+        if (has2) frag_axpy(gq, d2, k2);
+        if (far) frag_axpy(gq, dfw, kf);
         store_frag<TE, TMA>(dq + (long long)q * p.dq.sl, p.dq.sd, p.D, l, gq);
       }
-      if (act && l < 4) {
-        const float pv = l == 0 ? p0 : l == 1 ? p1 : l == 2 ? p2 : pf;
-        const float sv = l == 0 ? d0 : l == 1 ? d1 : l == 2 ? d2 : dfw;
-        E[c * 4 + l] = make_float2(pv, sv);
+      if (act && l == 0) {
+        E[c * 2] = make_float4(p0, d0, p1, d1);
+        E[c * 2 + 1] = make_float4(p2, d2, pf, dfw);
       }
     };
 
@@ -381,7 +408,7 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
       const int a = grp * 4;
       float lq[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) lq[i] = (j0 + a + i < p.L) ? lse[j0 + a + i] : 0.f;
+      for (int i = 0; i < 4; ++i) lq[i] = (j0 + a + i < p.L) ? lse[j0 + a + i] * kLog2e : 0.f;
       Frag k1 = FragIO<TE>::load(KN + (a + Hc - 1) * P, l), k2 = FragIO<TE>::load(KN + (a + Hc - 2) * P, l);
       Frag v1 = FragIO<TE>::load(VN + (a + Hc - 1) * P, l), v2 = FragIO<TE>::load(VN + (a + Hc - 2) * P, l);
 #pragma unroll
@@ -411,7 +438,7 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
         for (int i = 0; i < xr; ++i) {
           const bool act = e0 + i < Hc;
           const int c = act ? T + e0 + i : cbase;
-          const float lq = (act && j0 + c < p.L) ? lse[j0 + c] : 0.f;
+          const float lq = (act && j0 + c < p.L) ? lse[j0 + c] * kLog2e : 0.f;
           const Frag k0 = FragIO<TE>::load(KN + (c + Hc) * P, l);
           const Frag v0 = FragIO<TE>::load(VN + (c + Hc) * P, l);
           consume(c, act, k0, v0, k1, v1, k2, v2, lq);
@@ -423,9 +450,16 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
       }
     }
     __syncthreads();
+    // Phase 2 reads no K/V: the next step's K/V copies go out now.
+    if constexpr (TMA) {
+      if (tid == 0 && step + 1 < n_steps) issue_kv(step + 1);
+    } else {
+      __syncthreads();
+    }
 
     // ---- Phase 2: dK / dV of own keys, gathered from their consumers. ----
     {
+      const float2* E2 = reinterpret_cast<const float2*>(E);  // [c][4] (p, ds) per source
       const int a = grp * 4;
       Frag q1 = FragIO<TE>::load(Qs + (a + 1) * P, l), d1 = FragIO<TE>::load(Ds + (a + 1) * P, l);
       Frag q0 = FragIO<TE>::load(Qs + a * P, l), d0 = FragIO<TE>::load(Ds + a * P, l);
@@ -436,40 +470,37 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
         const Frag d2 = FragIO<TE>::load(Ds + (r + 2) * P, l);
         if (!is_pre) {
           Frag ak = carry_k[i], av = carry_v[i];
-          if (g.has0) {
-            const float2 e = E[r * 4 + 0];
+          if (has0) {
+            const float2 e = E2[r * 4 + 0];
             frag_axpy(ak, e.y, q0);
             frag_axpy(av, e.x, d0);
           }
-          if (g.has1) {
-            const float2 e = E[(r + 1) * 4 + 1];
+          if (has1) {
+            const float2 e = E2[(r + 1) * 4 + 1];
             frag_axpy(ak, e.y, q1);
             frag_axpy(av, e.x, d1);
           }
-          if (g.has2) {
-            const float2 e = E[(r + 2) * 4 + 2];
+          if (has2) {
+            const float2 e = E2[(r + 2) * 4 + 2];
             frag_axpy(ak, e.y, q2);
             frag_axpy(av, e.x, d2);
           }
           if (far && !chain) {
             const int c = r + d;
-            const float2 e = E[c * 4 + 3];
+            const float2 e = E2[c * 4 + 3];
             frag_axpy(ak, e.y, FragIO<TE>::load(Qs + c * P, l));
             frag_axpy(av, e.x, FragIO<TE>::load(Ds + c * P, l));
           }
           const int j = j0 + r;
           if (j < p.L) {
-            frag_scale(ak, scale);
             store_frag<TE, TMA>(dk + (long long)j * p.dk.sl, p.dk.sd, p.D, l, ak);
             store_frag<TE, TMA>(dv + (long long)j * p.dv.sl, p.dv.sd, p.D, l, av);
           }
         }
         if (chain && far) {
-          const float2 e = E[r * 4 + 3];
-          carry_k[i] = frag_zero();
-          carry_v[i] = frag_zero();
-          frag_axpy(carry_k[i], e.y, q0);
-          frag_axpy(carry_v[i], e.x, d0);
+          const float2 e = E2[r * 4 + 3];
+          carry_k[i] = frag_mul(e.y, q0);
+          carry_v[i] = frag_mul(e.x, d0);
         }
         q0 = q1;
         d0 = d1;
@@ -477,7 +508,7 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
         d1 = d2;
       }
     }
-    __syncthreads();  // slots of this step are refilled two steps later
+    __syncthreads();  // slots of this step are refilled by later copies
   }
 }
 
@@ -485,9 +516,9 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_v2_kernel(const __grid_cons
 // Launchers
 // --------------------------------------------------------------------------
 
-template <typename TE, int LPR, bool TMA>
+template <typename TE, int LPR, bool TMA, int SHAPE>
 int launch_fwd_v2(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
-  auto kern = sbda_fwd_v2_kernel<TE, LPR, TMA>;
+  auto kern = sbda_fwd_v2_kernel<TE, LPR, TMA, SHAPE>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_fwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
   const long long blocks = (long long)p.B * p.H * pl.g.nT;
@@ -495,9 +526,9 @@ int launch_fwd_v2(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, c
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
-template <typename TE, int LPR, bool TMA>
+template <typename TE, int LPR, bool TMA, int SHAPE>
 int launch_bwd_v2(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
-  auto kern = sbda_bwd_v2_kernel<TE, LPR, TMA>;
+  auto kern = sbda_bwd_v2_kernel<TE, LPR, TMA, SHAPE>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
   kern<<<pl.blocks_bwd, kThreads, pl.smem_bwd, st>>>(maps, p);
@@ -506,21 +537,49 @@ int launch_bwd_v2(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, c
 
 template <typename TE, bool TMA>
 int fwd_v2_lpr(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
-  if constexpr (sizeof(TE) == 4) {
-    if (pl.lpr == 4) return launch_fwd_v2<TE, 4, TMA>(maps, p, pl, st);
+  if constexpr (TMA) {
+    if (pl.lpr == 8) {
+      const V2Geometry& g = pl.g;
+      if (g.has0 && g.has1 && !g.has2 && !g.has_far) return launch_fwd_v2<TE, 8, TMA, 1>(maps, p, pl, st);
+      if (g.has0 && !g.has1 && g.has2 && !g.has_far) return launch_fwd_v2<TE, 8, TMA, 2>(maps, p, pl, st);
+      if (g.has0 && g.has1 && g.has2 && g.has_far) return launch_fwd_v2<TE, 8, TMA, 3>(maps, p, pl, st);
+    }
   }
-  if (pl.lpr == 8) return launch_fwd_v2<TE, 8, TMA>(maps, p, pl, st);
-  if (pl.lpr == 16) return launch_fwd_v2<TE, 16, TMA>(maps, p, pl, st);
+  if constexpr (sizeof(TE) == 4) {
+    if (pl.lpr == 4) return launch_fwd_v2<TE, 4, TMA, 0>(maps, p, pl, st);
+  }
+  if (pl.lpr == 8) return launch_fwd_v2<TE, 8, TMA, 0>(maps, p, pl, st);
+  if (pl.lpr == 16) return launch_fwd_v2<TE, 16, TMA, 0>(maps, p, pl, st);
   return SBDA_ERR_UNSUPPORTED;
+}
+
+// Source-set shape of a plan (see BwdShape); 0 when no specialisation applies.
+int bwd_shape(const V2Geometry& g) {
+  if (g.has0 && g.has1 && !g.has2 && !g.has_far) return 1;
+  if (g.has0 && !g.has1 && g.has2 && !g.has_far) return 2;
+  if (g.has0 && g.has1 && g.has2 && g.has_far) return g.mode == 0 ? 4 : 3;
+  return 0;
 }
 
 template <typename TE, bool TMA>
 int bwd_v2_lpr(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
-  if constexpr (sizeof(TE) == 4) {
-    if (pl.lpr == 4) return launch_bwd_v2<TE, 4, TMA>(maps, p, pl, st);
+  // Specialised shapes are compiled for the copy-engine path at 8 lanes per row.
+  if constexpr (TMA) {
+    if (pl.lpr == 8) {
+      switch (bwd_shape(pl.g)) {
+        case 1: return launch_bwd_v2<TE, 8, TMA, 1>(maps, p, pl, st);
+        case 2: return launch_bwd_v2<TE, 8, TMA, 2>(maps, p, pl, st);
+        case 3: return launch_bwd_v2<TE, 8, TMA, 3>(maps, p, pl, st);
+        case 4: return launch_bwd_v2<TE, 8, TMA, 4>(maps, p, pl, st);
+        default: break;
+      }
+    }
   }
-  if (pl.lpr == 8) return launch_bwd_v2<TE, 8, TMA>(maps, p, pl, st);
-  if (pl.lpr == 16) return launch_bwd_v2<TE, 16, TMA>(maps, p, pl, st);
+  if constexpr (sizeof(TE) == 4) {
+    if (pl.lpr == 4) return launch_bwd_v2<TE, 4, TMA, 0>(maps, p, pl, st);
+  }
+  if (pl.lpr == 8) return launch_bwd_v2<TE, 8, TMA, 0>(maps, p, pl, st);
+  if (pl.lpr == 16) return launch_bwd_v2<TE, 16, TMA, 0>(maps, p, pl, st);
   return SBDA_ERR_UNSUPPORTED;
 }
 
