@@ -110,6 +110,36 @@ int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int3
                        void* stream);
 
 /*
+ * Per-head RMSNorm + half-split RoPE of q or k, forward.  Replaces the eager
+ * _HeadRMSNorm + _apply_rope of BiAttn/attention_common.py:13-76 as applied
+ * at BiAttn/left_v2.py:237-239.  x and y are [B, H, L, D] views (heads =
+ * shape.heads; kv_heads is ignored); weight is the fp32 [D] norm weight;
+ * cos_table / sin_table are [rows, D/2] in x's dtype (fp32 angles
+ * position * theta^(-2i/D) cast to the dtype, attention_common.py:13-22) and
+ * table row table_offset + l serves position l.  Odd D: norm only (no RoPE,
+ * tables may be NULL).  y may alias x.
+ */
+int sbda_b200_norm_rope_forward(int dtype, sbda_shape shape, sbda_tensor x, sbda_tensor y,
+                                const float* weight, float eps, const void* cos_table,
+                                const void* sin_table, int64_t table_offset, void* stream);
+
+/* fp32 floats of workspace sbda_b200_norm_rope_backward needs for `shape`. */
+int64_t sbda_b200_norm_rope_workspace_floats(sbda_shape shape);
+
+/*
+ * Backward of sbda_b200_norm_rope_forward: from x and grad_y writes grad_x
+ * (x's dtype) and grad_weight (fp32 [D], overwritten with the sum over all
+ * rows).  The caller provides `workspace` (>= the floats reported above) for
+ * the per-CTA weight-gradient partials; the reduction order is fixed, so
+ * results are bitwise reproducible.
+ */
+int sbda_b200_norm_rope_backward(int dtype, sbda_shape shape, sbda_tensor x, sbda_tensor grad_y,
+                                 const float* weight, float eps, const void* cos_table,
+                                 const void* sin_table, int64_t table_offset, sbda_tensor grad_x,
+                                 float* grad_weight, float* workspace, int64_t workspace_floats,
+                                 void* stream);
+
+/*
  * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
  * (the windowed chain-walking kernels wherever they apply, else the general
  * ones), 1 = general kernels only.  Returns the previous setting, or -1 for

@@ -286,6 +286,20 @@ def apply_rope(q: Tensor, k: Tensor, *, theta: float, position_offset: int = 0
     return q * qc + rotate_half(q) * qs, k * kc + rotate_half(k) * ks
 
 
+def apply_rope_table(x: Tensor, cos_half: Tensor, sin_half: Tensor) -> Tensor:
+    """RoPE of ``x`` ``[B,L,H,D]`` from explicit tables ``[L, D/2]``, computed in ``x.dtype``.
+
+    ``attention_common.py:48``: ``x * cat(cos, cos) + rotate_half(x) * cat(sin, sin)`` with the
+    tables already cast (``:20-21``).  Taking the tables as inputs lets a check use exactly the
+    table a device built (CPU and CUDA ``pow``/``cos`` differ in the last bit).
+    """
+    if x.shape[-1] % 2:
+        return x
+    cos = torch.cat((cos_half, cos_half), dim=-1)[None, :, None, :].to(x.dtype)
+    sin = torch.cat((sin_half, sin_half), dim=-1)[None, :, None, :].to(x.dtype)
+    return x * cos + rotate_half(x) * sin
+
+
 def norm_rope(q_raw: Tensor, k_raw: Tensor, q_weight: Tensor, k_weight: Tensor,
               *, theta: float = 1_000_000.0, eps: float = 1e-6,
               position_offset: int = 0) -> tuple[Tensor, Tensor]:
@@ -348,7 +362,7 @@ def algorithmic_bytes(rows: int, head_dim: int, elem_bytes: int, *, backward: bo
 __all__ = [
     "ORACLE_TOPOLOGIES", "unique_offsets", "schedule_offsets", "sbda_stage", "path_tensors",
     "exact_attention", "exact_lse", "exact_attention_grads", "query_rows", "key_rows", "head_rms_norm",
-    "rope_inverse_frequencies", "rope_cos_sin", "rotate_half", "apply_rope", "norm_rope",
+    "rope_inverse_frequencies", "rope_cos_sin", "rotate_half", "apply_rope", "apply_rope_table", "norm_rope",
     "module_forward", "algorithmic_bytes",
 ]
 

@@ -17,12 +17,13 @@ from .ops import (
     sbda_backward,
     sbda_forward,
 )
+from .norm_rope import norm_rope, rope_table
 from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_offsets
 
 __all__ = [
     "PATH_TOPOLOGIES", "SBDAttention", "SBDAAttention", "device_status", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
-    "fused_sbda_key_backward", "host_offsets", "sbda_attention", "sbda_backward", "sbda_forward",
+    "fused_sbda_key_backward", "host_offsets", "norm_rope", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
     "sbda_layer_offsets", "sbda_stage", "topology_offsets",
 ]
 

@@ -87,6 +87,18 @@ def load() -> ctypes.CDLL:
             SbdaTensor, SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
+        lib.sbda_b200_norm_rope_forward.restype = c_int
+        lib.sbda_b200_norm_rope_forward.argtypes = [
+            c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,
+            ctypes.c_int64, c_void_p,
+        ]
+        lib.sbda_b200_norm_rope_workspace_floats.restype = ctypes.c_int64
+        lib.sbda_b200_norm_rope_workspace_floats.argtypes = [SbdaShape]
+        lib.sbda_b200_norm_rope_backward.restype = c_int
+        lib.sbda_b200_norm_rope_backward.argtypes = [
+            c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,
+            ctypes.c_int64, SbdaTensor, c_void_p, c_void_p, ctypes.c_int64, c_void_p,
+        ]
         lib.sbda_b200_set_kernel_path.restype = c_int
         lib.sbda_b200_set_kernel_path.argtypes = [c_int]
         lib.sbda_b200_device_status.restype = c_int

@@ -13,12 +13,17 @@ from __future__ import annotations
 import torch
 from torch import Tensor, nn
 
+from .norm_rope import norm_rope
 from .ops import _SBDAFunction, _check_inputs
 from .topology import PATH_TOPOLOGIES, topology_offsets
 
 
 class HeadRMSNorm(nn.Module):
-    """Per-head RMSNorm in fp32 with a learned weight (``attention_common.py:64-76``)."""
+    """Holds the per-head RMSNorm weight (``attention_common.py:64-76``).
+
+    ``forward`` is the eager formula, kept for callers that use the norm on
+    its own; ``SBDAttention`` applies norm and RoPE through ``norm_rope``.
+    """
 
     def __init__(self, dim: int, eps: float = 1e-6) -> None:
         super().__init__()
@@ -28,47 +33,6 @@ class HeadRMSNorm(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         normalized = x.float() * torch.rsqrt(x.float().pow(2).mean(dim=-1, keepdim=True) + self.eps)
         return (normalized * self.weight).to(dtype=x.dtype)
-
-
-_rope_cache: dict[tuple, tuple[Tensor, Tensor]] = {}
-
-
-def rope_tables(length: int, head_dim: int, theta: float, dtype: torch.dtype, device: torch.device,
-                position_offset: int = 0) -> tuple[Tensor, Tensor]:
-    """cos/sin ``[1, L, 1, D]`` in ``dtype`` from fp32 angles (``attention_common.py:13-22``).
-
-    Cached per (length, head_dim, theta, dtype, device, offset): every layer
-    of a stack shares one table.
-    """
-    key = (length, head_dim, float(theta), dtype, device, position_offset)
-    cached = _rope_cache.get(key)
-    if cached is not None:
-        return cached
-    indices = torch.arange(0, head_dim, 2, device=device, dtype=torch.float32)
-    inverse = theta ** (-indices / head_dim)
-    positions = torch.arange(length, device=device) + position_offset
-    angles = torch.outer(positions.to(torch.float32), inverse)
-    cos = torch.cat((angles.cos(), angles.cos()), dim=-1)[None, :, None, :].to(dtype)
-    sin = torch.cat((angles.sin(), angles.sin()), dim=-1)[None, :, None, :].to(dtype)
-    if len(_rope_cache) > 16:
-        _rope_cache.clear()
-    _rope_cache[key] = (cos, sin)
-    return cos, sin
-
-
-def apply_rope(q: Tensor, k: Tensor, *, theta: float, position_offset: int = 0) -> tuple[Tensor, Tensor]:
-    """Half-split RoPE on ``[B, L, H, D]`` (``attention_common.py:25-50``)."""
-    head_dim = q.shape[-1]
-    if head_dim % 2:
-        return q, k
-    half = head_dim // 2
-    qc, qs = rope_tables(q.shape[1], head_dim, theta, q.dtype, q.device, position_offset)
-    kc, ks = rope_tables(k.shape[1], head_dim, theta, k.dtype, k.device, position_offset)
-
-    def rotate(x: Tensor) -> Tensor:
-        return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
-
-    return q * qc + rotate(q) * qs, k * kc + rotate(k) * ks
 
 
 class SBDAttention(nn.Module):
@@ -138,9 +102,9 @@ class SBDAttention(nn.Module):
         q = self.q(x).view(batch, length, self.heads, self.head_dim)
         k = self.k(x).view(batch, length, self.kv_heads, self.head_dim)
         v = self.v(x).view(batch, length, self.kv_heads, self.head_dim)
-        q = self.q_norm(q)
-        k = self.k_norm(k)
-        q, k = apply_rope(q, k, theta=self.rope_theta)
+        # RMSNorm + RoPE on the B200 kernels (attention_common.py:25-76 semantics).
+        q = norm_rope(q, self.q_norm.weight, theta=self.rope_theta, eps=self.q_norm.eps)
+        k = norm_rope(k, self.k_norm.weight, theta=self.rope_theta, eps=self.k_norm.eps)
         q = q.permute(0, 2, 1, 3)
         k = k.permute(0, 2, 1, 3)
         v = v.permute(0, 2, 1, 3)

@@ -1,0 +1,336 @@
+// sbda_norm_rope.cu -- per-head RMSNorm + half-split RoPE for the SBDA q/k
+// projections, forward and backward, replacing the ~10 eager ops per tensor
+// of BiAttn/attention_common.py:13-76 (called at BiAttn/left_v2.py:237-239).
+//
+// Forward (per row = one head of one position, D channels, h = D / 2):
+//   r   = rsqrt(mean_j x_j^2 + eps)                         fp32 (attention_common.py:73-75)
+//   y_j = cast(x_j * r * w_j)                               cast to the input dtype (:76)
+//   z_j = cast(cast(y_j * c_j) + cast(rot(y)_j * s_j))      RoPE in the input dtype (:48-49)
+//   rot(y)_j = -y_{j+h} (j < h),  y_{j-h} (j >= h);  c, s = the position's cos/sin table row
+//   (fp32 angles cast to the input dtype, :13-22).  Odd D: z = y (:36-40).
+// Backward (fp32, the same function's exact derivative):
+//   g_j  = dz_j c_j + (j < h ? dz_{j+h} s_{j+h} : -dz_{j-h} s_{j-h})
+//   dx_k = r u_k - x_k r^3 (sum_j u_j x_j) / D,   u = g * w
+//   dw_j = sum over every row of g_j x_j r  -- per-CTA partial sums in a workspace
+//          and a fixed-order reduction: deterministic, no atomics.
+//
+// One thread owns one row.  A CTA stages 128 rows in shared memory with a
+// row pitch of D*e + 4 bytes (an odd number of words for even D), so the
+// lanes of a warp, reading the same channel of 32 consecutive rows, hit
+// distinct banks.  Staging loads/stores are warp-per-row and coalesced.
+// The backward is a fixed-size grid (at most kNRMaxCtas CTAs, independent
+// of the device) walking row blocks; each CTA keeps its weight-gradient
+// column sums and writes them once, so the final reduction is short and
+// its order is fixed.
+
+#include "sbda_common.cuh"
+
+namespace sbda {
+
+constexpr int kNRRows = 128;      // rows per CTA step (one per thread)
+constexpr int kNRMaxCtas = 1024;  // backward grid cap (partials per weight vector)
+
+struct NormRopeParams {
+  int B, L, H, D;
+  int rope;                 // 1 = apply RoPE (even D)
+  float eps;
+  TensorArg x;              // input rows [B, H, L, D]
+  TensorArg y;              // output rows (forward) / grad_x (backward)
+  TensorArg dy;             // backward: gradient of the rotated output
+  const float* w;           // [D] fp32 weight
+  const void* cos_t;        // [table rows, D/2] in the input dtype
+  const void* sin_t;
+  long long table_offset;   // table row of position 0
+  float* partial;           // backward: [gridDim.x, D] fp32 weight-gradient partials
+};
+
+template <typename TE>
+__device__ __forceinline__ float round_to(float x) {
+  return Elem<TE>::to_float(Elem<TE>::from_float(x));
+}
+
+// Row index -> (b, position, head); rows are ordered (b, position, head) so
+// that the heads of a position are neighbours (contiguous in [B, L, H, D]).
+__device__ __forceinline__ void row_coords(long long row, int L, int H, int& b, int& pos, int& h) {
+  h = (int)(row % H);
+  const long long bl = row / H;
+  pos = (int)(bl % L);
+  b = (int)(bl / L);
+}
+
+// Cooperative staging of a block of rows (warp per row, lanes over channels).
+template <typename TE>
+__device__ void stage_rows(TE* sm, int pitch, const TensorArg& t, long long row0, long long rows_total, int L,
+                           int H, int D) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const TE* src = reinterpret_cast<const TE*>(t.ptr);
+  for (int r = warp; r < kNRRows; r += nw) {
+    const long long row = row0 + r;
+    TE* dst = sm + r * pitch;
+    if (row < rows_total) {
+      int b, pos, h;
+      row_coords(row, L, H, b, pos, h);
+      const TE* s = src + (long long)b * t.sb + (long long)h * t.sh + (long long)pos * t.sl;
+      for (int c = lane; c < D; c += 32) dst[c] = s[(long long)c * t.sd];
+    } else {
+      for (int c = lane; c < D; c += 32) dst[c] = Elem<TE>::from_float(0.f);
+    }
+  }
+}
+
+template <typename TE>
+__device__ void unstage_rows(const TE* sm, int pitch, const TensorArg& t, long long row0, long long rows_total,
+                             int L, int H, int D) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  TE* dst0 = reinterpret_cast<TE*>(const_cast<void*>(t.ptr));
+  for (int r = warp; r < kNRRows; r += nw) {
+    const long long row = row0 + r;
+    if (row >= rows_total) break;
+    int b, pos, h;
+    row_coords(row, L, H, b, pos, h);
+    TE* d = dst0 + (long long)b * t.sb + (long long)h * t.sh + (long long)pos * t.sl;
+    const TE* s = sm + r * pitch;
+    for (int c = lane; c < D; c += 32) d[(long long)c * t.sd] = s[c];
+  }
+}
+
+template <typename TE>
+__global__ void __launch_bounds__(kNRRows) sbda_norm_rope_fwd_kernel(const NormRopeParams p) {
+  extern __shared__ __align__(16) uint8_t nr_smem[];
+  TE* sm = reinterpret_cast<TE*>(nr_smem);
+  const int D = p.D, pitch = D + 4 / (int)sizeof(TE), half = D / 2;
+  const long long rows_total = (long long)p.B * p.L * p.H;
+  const long long row0 = (long long)blockIdx.x * kNRRows;
+  stage_rows<TE>(sm, pitch, p.x, row0, rows_total, p.L, p.H, D);
+  __syncthreads();
+  const long long row = row0 + threadIdx.x;
+  if (row < rows_total) {
+    TE* xr = sm + threadIdx.x * pitch;
+    float ss = 0.f;
+    for (int j = 0; j < D; ++j) {
+      const float v = Elem<TE>::to_float(xr[j]);
+      ss = fmaf(v, v, ss);
+    }
+    const float r = rsqrtf(ss / (float)D + p.eps);
+    // y = cast(x * r * w), kept in place
+    for (int j = 0; j < D; ++j) xr[j] = Elem<TE>::from_float(Elem<TE>::to_float(xr[j]) * r * p.w[j]);
+    if (p.rope) {
+      int b, pos, h;
+      row_coords(row, p.L, p.H, b, pos, h);
+      const TE* ct = reinterpret_cast<const TE*>(p.cos_t) + (p.table_offset + pos) * half;
+      const TE* st = reinterpret_cast<const TE*>(p.sin_t) + (p.table_offset + pos) * half;
+      for (int j = 0; j < half; ++j) {
+        const float c = Elem<TE>::to_float(ct[j]), s = Elem<TE>::to_float(st[j]);
+        const float lo = Elem<TE>::to_float(xr[j]), hi = Elem<TE>::to_float(xr[j + half]);
+        // z_j = cast(cast(lo*c) + cast(-hi*s)); z_{j+h} = cast(cast(hi*c) + cast(lo*s))
+        const float zl = round_to<TE>(round_to<TE>(lo * c) + round_to<TE>(-hi * s));
+        const float zh = round_to<TE>(round_to<TE>(hi * c) + round_to<TE>(lo * s));
+        xr[j] = Elem<TE>::from_float(zl);
+        xr[j + half] = Elem<TE>::from_float(zh);
+      }
+    }
+  }
+  __syncthreads();
+  unstage_rows<TE>(sm, pitch, p.y, row0, rows_total, p.L, p.H, D);
+}
+
+template <typename TE>
+__global__ void __launch_bounds__(kNRRows) sbda_norm_rope_bwd_kernel(const NormRopeParams p) {
+  extern __shared__ __align__(16) uint8_t nr_smem[];
+  const int D = p.D, pitch = D + 4 / (int)sizeof(TE), half = D / 2;
+  TE* sx = reinterpret_cast<TE*>(nr_smem);
+  TE* sg = sx + kNRRows * pitch;
+  float* contrib = reinterpret_cast<float*>(sg + kNRRows * pitch);  // [kNRRows][D + 1]
+  const int cpitch = D + 1;
+  const long long rows_total = (long long)p.B * p.L * p.H;
+  const long long nblocks = (rows_total + kNRRows - 1) / kNRRows;
+  float* cr = contrib + threadIdx.x * cpitch;
+  for (int j = 0; j < D; ++j) cr[j] = 0.f;
+  for (long long blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const long long row0 = blk * kNRRows;
+    __syncthreads();  // staging buffers of the previous block are drained
+    stage_rows<TE>(sx, pitch, p.x, row0, rows_total, p.L, p.H, D);
+    stage_rows<TE>(sg, pitch, p.dy, row0, rows_total, p.L, p.H, D);
+    __syncthreads();
+    const long long row = row0 + threadIdx.x;
+    if (row < rows_total) {
+      TE* xr = sx + threadIdx.x * pitch;
+      TE* gr = sg + threadIdx.x * pitch;
+      float ss = 0.f;
+      for (int j = 0; j < D; ++j) {
+        const float v = Elem<TE>::to_float(xr[j]);
+        ss = fmaf(v, v, ss);
+      }
+      const float r = rsqrtf(ss / (float)D + p.eps);
+      // Two passes over the row: g = RoPE-transposed gradient (recomputed in
+      // the second pass rather than stored), dot = sum(g * w * x), then dx.
+      float dot = 0.f;
+      if (p.rope) {
+        int b, pos, h;
+        row_coords(row, p.L, p.H, b, pos, h);
+        const TE* ct = reinterpret_cast<const TE*>(p.cos_t) + (p.table_offset + pos) * half;
+        const TE* st = reinterpret_cast<const TE*>(p.sin_t) + (p.table_offset + pos) * half;
+        for (int j = 0; j < half; ++j) {
+          const float c = Elem<TE>::to_float(ct[j]), s = Elem<TE>::to_float(st[j]);
+          const float dl = Elem<TE>::to_float(gr[j]), dh = Elem<TE>::to_float(gr[j + half]);
+          const float gl = dl * c + dh * s, gh = dh * c - dl * s;
+          const float xl = Elem<TE>::to_float(xr[j]), xh = Elem<TE>::to_float(xr[j + half]);
+          dot = fmaf(gl * p.w[j], xl, dot);
+          dot = fmaf(gh * p.w[j + half], xh, dot);
+          cr[j] = fmaf(gl * xl, r, cr[j]);
+          cr[j + half] = fmaf(gh * xh, r, cr[j + half]);
+        }
+        const float k3 = r * r * r * dot / (float)D;
+        for (int j = 0; j < half; ++j) {
+          const float c = Elem<TE>::to_float(ct[j]), s = Elem<TE>::to_float(st[j]);
+          const float dl = Elem<TE>::to_float(gr[j]), dh = Elem<TE>::to_float(gr[j + half]);
+          const float gl = dl * c + dh * s, gh = dh * c - dl * s;
+          const float xl = Elem<TE>::to_float(xr[j]), xh = Elem<TE>::to_float(xr[j + half]);
+          gr[j] = Elem<TE>::from_float(r * gl * p.w[j] - xl * k3);
+          gr[j + half] = Elem<TE>::from_float(r * gh * p.w[j + half] - xh * k3);
+        }
+      } else {
+        for (int j = 0; j < D; ++j) {
+          const float g = Elem<TE>::to_float(gr[j]), x = Elem<TE>::to_float(xr[j]);
+          dot = fmaf(g * p.w[j], x, dot);
+          cr[j] = fmaf(g * x, r, cr[j]);
+        }
+        const float k3 = r * r * r * dot / (float)D;
+        for (int j = 0; j < D; ++j) {
+          const float g = Elem<TE>::to_float(gr[j]), x = Elem<TE>::to_float(xr[j]);
+          gr[j] = Elem<TE>::from_float(r * g * p.w[j] - x * k3);
+        }
+      }
+    }
+    __syncthreads();
+    unstage_rows<TE>(sg, pitch, p.y, row0, rows_total, p.L, p.H, D);
+  }
+  __syncthreads();
+  // Fixed-order column sums of this CTA's rows -> partial[blockIdx.x][j].
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float acc = 0.f;
+    for (int rr = 0; rr < kNRRows; ++rr) acc += contrib[rr * cpitch + j];
+    p.partial[(long long)blockIdx.x * D + j] = acc;
+  }
+}
+
+// dw[j] = sum over blocks (fixed order) of partial[block][j].
+__global__ void sbda_norm_weight_reduce_kernel(const float* __restrict__ partial, int blocks, int D,
+                                               float* __restrict__ dw) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= D) return;
+  float acc = 0.f;
+  for (int b = 0; b < blocks; ++b) acc += partial[(long long)b * D + j];
+  dw[j] = acc;
+}
+
+template <typename TE>
+int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
+  const size_t smem = (size_t)kNRRows * (p.D * sizeof(TE) + 4);
+  auto kern = sbda_norm_rope_fwd_kernel<TE>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SBDA_ERR_CUDA;
+  kern<<<blocks, kNRRows, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+}
+
+template <typename TE>
+int nr_backward(const NormRopeParams& p, unsigned blocks, float* grad_w, cudaStream_t st) {
+  const size_t smem = (size_t)kNRRows * (2 * (p.D * sizeof(TE) + 4) + (p.D + 1) * sizeof(float));
+  auto kern = sbda_norm_rope_bwd_kernel<TE>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SBDA_ERR_CUDA;
+  kern<<<blocks, kNRRows, smem, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return SBDA_ERR_CUDA;
+  sbda_norm_weight_reduce_kernel<<<(p.D + 127) / 128, 128, 0, st>>>(p.partial, (int)blocks, p.D, grad_w);
+  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+}
+
+int64_t norm_rope_blocks(const sbda_shape& s) {
+  const int64_t rows = s.batch * s.length * s.heads;
+  return (rows + kNRRows - 1) / kNRRows;
+}
+
+// Backward grid: one CTA per row block up to kNRMaxCtas (device-independent,
+// so the weight-gradient summation order is too).
+int64_t norm_rope_bwd_ctas(const sbda_shape& s) {
+  const int64_t b = norm_rope_blocks(s);
+  return b < kNRMaxCtas ? b : kNRMaxCtas;
+}
+
+int norm_rope_check(int dtype, const sbda_shape& s, float eps) {
+  if (dtype != SBDA_DTYPE_F32 && dtype != SBDA_DTYPE_F16 && dtype != SBDA_DTYPE_BF16) return SBDA_ERR_DTYPE;
+  if (s.batch < 0 || s.heads < 0 || s.length < 0 || s.head_dim < 1 || s.head_dim > 128) return SBDA_ERR_INVALID;
+  if (!(eps >= 0.f)) return SBDA_ERR_INVALID;
+  if (s.length > ((int64_t)1 << 31) - 1 || norm_rope_blocks(s) > ((int64_t)1 << 31) - 1) return SBDA_ERR_UNSUPPORTED;
+  return SBDA_OK;
+}
+
+NormRopeParams nr_params(const sbda_shape& s, const sbda_tensor& x, const sbda_tensor& y, const float* w,
+                         float eps, const void* cos_t, const void* sin_t, int64_t table_offset) {
+  NormRopeParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = (int)s.batch;
+  p.L = (int)s.length;
+  p.H = (int)s.heads;
+  p.D = (int)s.head_dim;
+  p.rope = (s.head_dim % 2 == 0) && cos_t && sin_t;
+  p.eps = eps;
+  p.x = TensorArg{x.data, x.stride_b, x.stride_h, x.stride_l, x.stride_d};
+  p.y = TensorArg{y.data, y.stride_b, y.stride_h, y.stride_l, y.stride_d};
+  p.w = w;
+  p.cos_t = cos_t;
+  p.sin_t = sin_t;
+  p.table_offset = table_offset;
+  return p;
+}
+
+}  // namespace sbda
+
+using namespace sbda;
+
+extern "C" int64_t sbda_b200_norm_rope_workspace_floats(sbda_shape shape) {
+  if (shape.head_dim < 1 || shape.batch < 0 || shape.heads < 0 || shape.length < 0) return 0;
+  return norm_rope_bwd_ctas(shape) * shape.head_dim;
+}
+
+extern "C" int sbda_b200_norm_rope_forward(int dtype, sbda_shape shape, sbda_tensor x, sbda_tensor y,
+                                           const float* weight, float eps, const void* cos_table,
+                                           const void* sin_table, int64_t table_offset, void* stream) {
+  int st = norm_rope_check(dtype, shape, eps);
+  if (st != SBDA_OK) return st;
+  if (shape.batch == 0 || shape.heads == 0 || shape.length == 0) return SBDA_OK;
+  if (!x.data || !y.data || !weight) return SBDA_ERR_INVALID;
+  if (shape.head_dim % 2 == 0 && (!cos_table || !sin_table)) return SBDA_ERR_INVALID;
+  const NormRopeParams p = nr_params(shape, x, y, weight, eps, cos_table, sin_table, table_offset);
+  const unsigned blocks = (unsigned)norm_rope_blocks(shape);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == SBDA_DTYPE_F32) return nr_forward<float>(p, blocks, s);
+  if (dtype == SBDA_DTYPE_F16) return nr_forward<__half>(p, blocks, s);
+  return nr_forward<__nv_bfloat16>(p, blocks, s);
+}
+
+extern "C" int sbda_b200_norm_rope_backward(int dtype, sbda_shape shape, sbda_tensor x, sbda_tensor grad_y,
+                                            const float* weight, float eps, const void* cos_table,
+                                            const void* sin_table, int64_t table_offset, sbda_tensor grad_x,
+                                            float* grad_weight, float* workspace, int64_t workspace_floats,
+                                            void* stream) {
+  int st = norm_rope_check(dtype, shape, eps);
+  if (st != SBDA_OK) return st;
+  if (!grad_weight) return SBDA_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (shape.batch == 0 || shape.heads == 0 || shape.length == 0) {
+    return cudaMemsetAsync(grad_weight, 0, sizeof(float) * shape.head_dim, s) == cudaSuccess ? SBDA_OK
+                                                                                             : SBDA_ERR_CUDA;
+  }
+  if (!x.data || !grad_y.data || !grad_x.data || !weight || !workspace) return SBDA_ERR_INVALID;
+  if (shape.head_dim % 2 == 0 && (!cos_table || !sin_table)) return SBDA_ERR_INVALID;
+  if (workspace_floats < sbda_b200_norm_rope_workspace_floats(shape)) return SBDA_ERR_INVALID;
+  NormRopeParams p = nr_params(shape, x, grad_x, weight, eps, cos_table, sin_table, table_offset);
+  p.dy = TensorArg{grad_y.data, grad_y.stride_b, grad_y.stride_h, grad_y.stride_l, grad_y.stride_d};
+  p.partial = workspace;
+  const unsigned blocks = (unsigned)norm_rope_bwd_ctas(shape);
+  if (dtype == SBDA_DTYPE_F32) return nr_backward<float>(p, blocks, grad_weight, s);
+  if (dtype == SBDA_DTYPE_F16) return nr_backward<__half>(p, blocks, grad_weight, s);
+  return nr_backward<__nv_bfloat16>(p, blocks, grad_weight, s);
+}

@@ -101,3 +101,21 @@ def test_python_errors_follow_reference_types():
         sbda_b200.SBDAttention(16, 2, 3, use_fused=False)
     assert set(module.state_dict()) == {"q.weight", "k.weight", "v.weight", "out.weight",
                                         "q_norm.weight", "k_norm.weight"}
+
+
+def test_norm_rope_validation_codes(lib):
+    t = _lib.SbdaTensor(16, 1 << 20, 64, 256, 1)
+    s = _lib.SbdaShape(1, 4, 4, 1000, 64)
+    fwd = lib.sbda_b200_norm_rope_forward
+    assert fwd(9, s, t, t, 16, 1e-6, 16, 16, 0, None) == _lib.SBDA_ERR_DTYPE
+    assert fwd(2, _lib.SbdaShape(1, 4, 4, 1000, 129), t, t, 16, 1e-6, 16, 16, 0, None) == _lib.SBDA_ERR_INVALID
+    assert fwd(2, s, t, t, 16, -1.0, 16, 16, 0, None) == _lib.SBDA_ERR_INVALID
+    assert fwd(2, s, t, t, None, 1e-6, 16, 16, 0, None) == _lib.SBDA_ERR_INVALID
+    assert fwd(2, s, t, t, 16, 1e-6, None, 16, 0, None) == _lib.SBDA_ERR_INVALID  # even D needs tables
+    assert fwd(2, _lib.SbdaShape(1, 4, 4, 0, 64), t, t, 16, 1e-6, 16, 16, 0, None) == _lib.SBDA_OK
+    # one partial row of fp32 per CTA of 128 rows, capped at 1024 CTAs
+    assert lib.sbda_b200_norm_rope_workspace_floats(s) == 32 * 64
+    assert lib.sbda_b200_norm_rope_workspace_floats(_lib.SbdaShape(8, 8, 8, 1 << 20, 64)) == 1024 * 64
+    bwd = lib.sbda_b200_norm_rope_backward
+    assert bwd(2, s, t, t, 16, 1e-6, 16, 16, 0, t, 16, 16, 2047, None) == _lib.SBDA_ERR_INVALID  # workspace
+    assert bwd(2, s, t, t, 16, 1e-6, 16, 16, 0, t, None, 16, 2048, None) == _lib.SBDA_ERR_INVALID
