@@ -140,6 +140,24 @@ int sbda_b200_norm_rope_backward(int dtype, sbda_shape shape, sbda_tensor x, sbd
                                  void* stream);
 
 /*
+ * Allocation-free variant of sbda_b200_norm_rope_backward.  It has no
+ * counterpart in the reference.  It exists for callers that cannot allocate
+ * device memory where the backward runs (a replayed graph with a fixed pool,
+ * a runtime or plugin host that only hands out tensors it planned): instead
+ * of a caller workspace it uses a 512 KiB static device array that every GPU
+ * loading this library holds until exit.  Shapes whose partials would not
+ * fit are rejected with SBDA_ERR_UNSUPPORTED (none of the shapes the
+ * backward accepts do today).  The first call on each device resolves the
+ * array's device address; make that first call before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU race: run them
+ * one after another.  Results are identical to sbda_b200_norm_rope_backward.
+ */
+int sbda_b200_norm_rope_backward_noalloc(int dtype, sbda_shape shape, sbda_tensor x, sbda_tensor grad_y,
+                                         const float* weight, float eps, const void* cos_table,
+                                         const void* sin_table, int64_t table_offset,
+                                         sbda_tensor grad_x, float* grad_weight, void* stream);
+
+/*
  * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
  * (the windowed chain-walking kernels wherever they apply, else the general
  * ones), 1 = general kernels only.  Returns the previous setting, or -1 for

@@ -99,6 +99,11 @@ def load() -> ctypes.CDLL:
             c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,
             ctypes.c_int64, SbdaTensor, c_void_p, c_void_p, ctypes.c_int64, c_void_p,
         ]
+        lib.sbda_b200_norm_rope_backward_noalloc.restype = c_int
+        lib.sbda_b200_norm_rope_backward_noalloc.argtypes = [
+            c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,
+            ctypes.c_int64, SbdaTensor, c_void_p, c_void_p,
+        ]
         lib.sbda_b200_set_kernel_path.restype = c_int
         lib.sbda_b200_set_kernel_path.argtypes = [c_int]
         lib.sbda_b200_device_status.restype = c_int

@@ -25,6 +25,8 @@
 
 #include "sbda_common.cuh"
 
+#include <atomic>
+
 namespace sbda {
 
 constexpr int kNRRows = 128;      // rows per CTA step (one per thread)
@@ -329,6 +331,81 @@ extern "C" int sbda_b200_norm_rope_backward(int dtype, sbda_shape shape, sbda_te
   NormRopeParams p = nr_params(shape, x, grad_x, weight, eps, cos_table, sin_table, table_offset);
   p.dy = TensorArg{grad_y.data, grad_y.stride_b, grad_y.stride_h, grad_y.stride_l, grad_y.stride_d};
   p.partial = workspace;
+  const unsigned blocks = (unsigned)norm_rope_bwd_ctas(shape);
+  if (dtype == SBDA_DTYPE_F32) return nr_backward<float>(p, blocks, grad_weight, s);
+  if (dtype == SBDA_DTYPE_F16) return nr_backward<__half>(p, blocks, grad_weight, s);
+  return nr_backward<__nv_bfloat16>(p, blocks, grad_weight, s);
+}
+
+// --------------------------------------------------------------------------
+// Allocation-free backward.
+//
+// Some callers cannot allocate device memory at the point where they run
+// the backward: code replayed inside a captured CUDA graph whose memory pool
+// is fixed, custom runtimes that hand out only the tensors they planned, or
+// plugin hosts that forbid allocation in the execution callback.  For them
+// the weight-gradient partials live in this file-scope array instead of a
+// caller workspace.  It holds kNoAllocScratchFloats floats (512 KiB: 1024
+// CTAs x 128 channels, enough for every shape the backward accepts) on every
+// GPU that loads the library, until the process exits.
+//
+// Every call shares the array.  Each CTA overwrites its partial row before
+// the reduction reads it, so nothing needs clearing between calls, but two
+// calls that overlap on the GPU (different streams, or different host
+// threads on one device) race on it: serialise them.
+// --------------------------------------------------------------------------
+
+namespace sbda {
+
+constexpr int64_t kNoAllocScratchFloats = (int64_t)kNRMaxCtas * 128;
+
+static __device__ __align__(256) float g_norm_rope_scratch[kNoAllocScratchFloats];
+
+// Device address of g_norm_rope_scratch for the current device, resolved
+// once per device (the host-side symbol is not a device pointer).
+float* norm_rope_scratch_ptr(int* status) {
+  static std::atomic<float*> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = SBDA_ERR_CUDA;
+    return nullptr;
+  }
+  float* p = cache[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_norm_rope_scratch) != cudaSuccess || !addr) {
+    *status = SBDA_ERR_CUDA;
+    return nullptr;
+  }
+  cache[dev].store(static_cast<float*>(addr), std::memory_order_release);
+  return static_cast<float*>(addr);
+}
+
+}  // namespace sbda
+
+extern "C" int sbda_b200_norm_rope_backward_noalloc(int dtype, sbda_shape shape, sbda_tensor x,
+                                                    sbda_tensor grad_y, const float* weight, float eps,
+                                                    const void* cos_table, const void* sin_table,
+                                                    int64_t table_offset, sbda_tensor grad_x,
+                                                    float* grad_weight, void* stream) {
+  int st = norm_rope_check(dtype, shape, eps);
+  if (st != SBDA_OK) return st;
+  if (!grad_weight) return SBDA_ERR_INVALID;
+  const int64_t need = sbda_b200_norm_rope_workspace_floats(shape);
+  if (need > kNoAllocScratchFloats) return SBDA_ERR_UNSUPPORTED;  // beyond the static scratch
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (shape.batch == 0 || shape.heads == 0 || shape.length == 0) {
+    return cudaMemsetAsync(grad_weight, 0, sizeof(float) * shape.head_dim, s) == cudaSuccess ? SBDA_OK
+                                                                                             : SBDA_ERR_CUDA;
+  }
+  if (!x.data || !grad_y.data || !grad_x.data || !weight) return SBDA_ERR_INVALID;
+  if (shape.head_dim % 2 == 0 && (!cos_table || !sin_table)) return SBDA_ERR_INVALID;
+  int status = SBDA_OK;
+  float* scratch = norm_rope_scratch_ptr(&status);
+  if (!scratch) return status;
+  NormRopeParams p = nr_params(shape, x, grad_x, weight, eps, cos_table, sin_table, table_offset);
+  p.dy = TensorArg{grad_y.data, grad_y.stride_b, grad_y.stride_h, grad_y.stride_l, grad_y.stride_d};
+  p.partial = scratch;
   const unsigned blocks = (unsigned)norm_rope_bwd_ctas(shape);
   if (dtype == SBDA_DTYPE_F32) return nr_backward<float>(p, blocks, grad_weight, s);
   if (dtype == SBDA_DTYPE_F16) return nr_backward<__half>(p, blocks, grad_weight, s);

@@ -1,0 +1,62 @@
+"""The allocation-free norm+RoPE backward gives the same results as the workspace one.
+
+``sbda_b200_norm_rope_backward_noalloc`` serves callers that cannot allocate device memory
+where the backward runs (a replayed graph with a fixed memory pool, a host runtime that only
+hands out tensors it planned): its weight-gradient partials live in a static device array of
+the library instead of a caller workspace.  This test drives both entry points through the
+C ABI on the same inputs, twice in a row with different data (the shared array keeps the
+previous call's partials), and requires the same outputs.  It lives in its own file, collected
+last, and needs nothing from the other test files.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import sbda_b200
+from sbda_b200 import _lib
+from sbda_b200.norm_rope import _bhld_arg, _shape
+from sbda_b200.ops import _DTYPES
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(seed: int, dtype: torch.dtype):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = (torch.randn(2, 5000, 4, 64, device="cuda", generator=g) * 1.3).to(dtype)
+    dy = torch.randn(x.shape, device="cuda", generator=g).to(dtype)
+    w = (torch.rand(64, device="cuda", generator=g) + 0.5).contiguous()
+    cos, sin = sbda_b200.rope_table(5000, 64, 1e6, dtype, x.device)
+    return x, dy, w, cos, sin
+
+
+def _backward(lib, x, dy, w, cos, sin, *, noalloc: bool):
+    shape = _shape(x)
+    grad_x = torch.empty_like(x)
+    grad_w = torch.full((64,), float("nan"), device="cuda", dtype=torch.float32)
+    stream = torch.cuda.current_stream().cuda_stream
+    common = (_DTYPES[x.dtype], shape, _bhld_arg(x), _bhld_arg(dy), w.data_ptr(), 1e-6, cos.data_ptr(),
+              sin.data_ptr(), 0, _bhld_arg(grad_x), grad_w.data_ptr())
+    if noalloc:
+        status = lib.sbda_b200_norm_rope_backward_noalloc(*common, stream)
+    else:
+        workspace = torch.empty(lib.sbda_b200_norm_rope_workspace_floats(shape), device="cuda",
+                                dtype=torch.float32)
+        status = lib.sbda_b200_norm_rope_backward(*common, workspace.data_ptr(), workspace.numel(), stream)
+    assert status == _lib.SBDA_OK, _lib.status_string(status)
+    torch.cuda.synchronize()
+    return grad_x, grad_w
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_noalloc_backward_matches_workspace_backward_twice(dtype):
+    lib = _lib.load()
+    for seed in (1, 2):  # the second call runs over the first call's leftover partials
+        x, dy, w, cos, sin = _inputs(seed, dtype)
+        ref_x, ref_w = _backward(lib, x, dy, w, cos, sin, noalloc=False)
+        got_x, got_w = _backward(lib, x, dy, w, cos, sin, noalloc=True)
+        tol = dict(rtol=1e-5, atol=1e-5) if dtype == torch.float32 else dict(rtol=0.0, atol=2e-2)
+        torch.testing.assert_close(got_x.float(), ref_x.float(), **tol)
+        torch.testing.assert_close(got_w, ref_w, rtol=1e-5, atol=1e-5)
+    assert sbda_b200.device_status(reset=True) == 0
