@@ -110,6 +110,32 @@ int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int3
                        void* stream);
 
 /*
+ * Contiguous sequence shards (no counterpart in the reference, which is
+ * single-GPU; SURVEY row "sequence shards").  Rank r of `world` (<= 8) holds
+ * positions [r*L, (r+1)*L) of one sequence, L = shape.length, the same on
+ * every rank and a multiple of the tile height (64 for 16-bit D <= 64).  The
+ * far offset, if any, must also be a tile multiple.  k_ranks[i] / v_ranks[i]
+ * (and in the backward q, grad_out, lse) describe rank i's buffers as
+ * addresses valid on this GPU (peer memory mapped into this process, e.g.
+ * CUDA IPC or symmetric memory); the kernels stage remote rows over NVLink
+ * with non-multicast TMA, per tile, from the rank that owns them.  All peers'
+ * inputs must be complete before the call (a cross-rank barrier) and must not
+ * be overwritten until every rank's call has finished.  Outputs are this
+ * rank's rows only.  Same results as the single-GPU call on the whole
+ * sequence.
+ */
+int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                              float scale, int32_t rank, int32_t world, sbda_tensor q,
+                              const sbda_tensor* k_ranks, const sbda_tensor* v_ranks, sbda_tensor out,
+                              float* lse, void* stream);
+
+int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                               float scale, int32_t rank, int32_t world, const sbda_tensor* q_ranks,
+                               const sbda_tensor* k_ranks, const sbda_tensor* v_ranks,
+                               const sbda_tensor* grad_out_ranks, const float* const* lse_ranks,
+                               sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v, void* stream);
+
+/*
  * Per-head RMSNorm + half-split RoPE of q or k, forward.  Replaces the eager
  * _HeadRMSNorm + _apply_rope of BiAttn/attention_common.py:13-76 as applied
  * at BiAttn/left_v2.py:237-239.  x and y are [B, H, L, D] views (heads =

@@ -104,6 +104,18 @@ def load() -> ctypes.CDLL:
             c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,
             ctypes.c_int64, SbdaTensor, c_void_p, c_void_p,
         ]
+        tarr = ctypes.POINTER(SbdaTensor)
+        lib.sbda_b200_forward_sharded.restype = c_int
+        lib.sbda_b200_forward_sharded.argtypes = [
+            c_int, SbdaShape, i32p, c_int32, c_float, c_int32, c_int32,
+            SbdaTensor, tarr, tarr, SbdaTensor, c_void_p, c_void_p,
+        ]
+        lib.sbda_b200_backward_sharded.restype = c_int
+        lib.sbda_b200_backward_sharded.argtypes = [
+            c_int, SbdaShape, i32p, c_int32, c_float, c_int32, c_int32,
+            tarr, tarr, tarr, tarr, ctypes.POINTER(c_void_p),
+            SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
+        ]
         lib.sbda_b200_set_kernel_path.restype = c_int
         lib.sbda_b200_set_kernel_path.argtypes = [c_int]
         lib.sbda_b200_device_status.restype = c_int

@@ -293,6 +293,19 @@ TensorArg arg_of(const sbda_tensor& t) {
   return TensorArg{t.data, t.stride_b, t.stride_h, t.stride_l, t.stride_d};
 }
 
+// The whole sequence on one GPU.
+ShardInfo single_shard(int64_t L, const float* lse) {
+  ShardInfo s;
+  memset(&s, 0, sizeof(s));
+  s.rank = 0;
+  s.world = 1;
+  s.shard_len = (int)L;
+  s.pos0 = 0;
+  s.total_len = (int)L;
+  s.lse[0] = lse;
+  return s;
+}
+
 
 // Shape/stride eligibility shared by forward and backward.
 bool tensors_vector_ok(std::initializer_list<const sbda_tensor*> ts, int64_t B, int64_t L, int64_t D, int e,
@@ -389,6 +402,7 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
   p.out = arg_of(out);
   p.lse = lse;
   p.status = status_ptr();
+  p.sh = single_shard(L, lse);
   FwdMaps maps;
   memset(&maps, 0, sizeof(maps));
   bool tma = vec;
@@ -479,6 +493,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
   p.dv = arg_of(grad_v);
   p.lse = lse;
   p.status = status_ptr();
+  p.sh = single_shard(L, lse);
   BwdMaps maps;
   memset(&maps, 0, sizeof(maps));
   bool tma = vec;
@@ -507,4 +522,165 @@ extern "C" int sbda_b200_device_status(uint32_t* flags_out, int reset) {
   }
   if (flags_out) *flags_out = value;
   return value ? SBDA_ERR_DEVICE : SBDA_OK;
+}
+
+// --------------------------------------------------------------------------
+// Contiguous sequence shards
+// --------------------------------------------------------------------------
+
+namespace sbda {
+
+// Plan of a sharded call: the general kernels' tiling, linear tile order, and
+// every staged region inside one rank (shards and the far offset are tile
+// multiples).  Returns a status.
+int plan_sharded(const int32_t* offsets, int n, int64_t Ls, int64_t D, int e, int world, Plan* pl) {
+  const int st = make_plan(offsets, n, Ls, D, e, pl);
+  if (st != SBDA_OK) return st;
+  if (world < 1 || world > kMaxShards) return SBDA_ERR_INVALID;
+  if (Ls % pl->tile) return SBDA_ERR_UNSUPPORTED;
+  if (pl->g.has_far && pl->g.f % pl->tile) return SBDA_ERR_UNSUPPORTED;
+  if (pl->g.Hn > Ls) return SBDA_ERR_UNSUPPORTED;
+  if ((int64_t)world * Ls > ((int64_t)1 << 31) - 1) return SBDA_ERR_UNSUPPORTED;
+  pl->g.R = pl->g.A = pl->g.rem = 0;  // the far tile may live on another GPU: plain tile order
+  return SBDA_OK;
+}
+
+ShardInfo shard_info(int rank, int world, int64_t Ls) {
+  ShardInfo s;
+  memset(&s, 0, sizeof(s));
+  s.rank = rank;
+  s.world = world;
+  s.shard_len = (int)Ls;
+  s.pos0 = (int)(rank * Ls);
+  s.total_len = (int)(world * Ls);
+  return s;
+}
+
+// Encodes one map per rank; all ranks' buffers must share one layout.
+bool encode_ranks(CUtensorMap* maps, unsigned* slots, const sbda_tensor* ts, int world, int dtype, int64_t B,
+                  int64_t H, int64_t L, int64_t D, int pitch, int rows) {
+  unsigned first = 0;
+  for (int r = 0; r < world; ++r) {
+    unsigned s = 0;
+    if (!vector_ok(ts[r], B, H, L, D, elem_size(dtype))) return false;
+    if (!encode_map(&maps[r], &s, ts[r], dtype, B, H, L, D, pitch, rows)) return false;
+    if (r == 0) first = s;
+    else if (s != first) return false;
+  }
+  if (slots) *slots = first;
+  return true;
+}
+
+}  // namespace sbda
+
+extern "C" int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                         float scale, int32_t rank, int32_t world, sbda_tensor q,
+                                         const sbda_tensor* k_ranks, const sbda_tensor* v_ranks, sbda_tensor out,
+                                         float* lse, void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  if (world < 1 || world > kMaxShards || rank < 0 || rank >= world || !k_ranks || !v_ranks)
+    return SBDA_ERR_INVALID;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, Ls = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || Ls == 0) return SBDA_OK;
+  if (!q.data || !out.data || !lse) return SBDA_ERR_INVALID;
+  for (int r = 0; r < world; ++r)
+    if (!k_ranks[r].data || !v_ranks[r].data) return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  Plan pl;
+  st = plan_sharded(offsets, n_offsets, Ls, D, e, world, &pl);
+  if (st != SBDA_OK) return st;
+  if (!vector_ok(q, B, H, Ls, D, e) || !vector_ok(out, B, H, Ls, D, e)) return SBDA_ERR_UNSUPPORTED;
+
+  FwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = (int)B;
+  p.H = (int)H;
+  p.Hkv = (int)Hkv;
+  p.G = (int)(H / Hkv);
+  p.L = (int)Ls;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = pl.g;
+  p.q = arg_of(q);
+  p.k = arg_of(k_ranks[rank]);
+  p.v = arg_of(v_ranks[rank]);
+  p.out = arg_of(out);
+  p.lse = lse;
+  p.status = status_ptr();
+  p.sh = shard_info(rank, world, Ls);
+  p.sh.lse[rank] = lse;
+
+  ShardFwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  bool ok = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, Ls, D, pl.pitch, pl.tile) &&
+            encode_ranks(maps.kT, &p.slots_k, k_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.tile) &&
+            encode_ranks(maps.vT, &p.slots_v, v_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.tile);
+  if (ok && pl.g.Hn > 0)
+    ok = encode_ranks(maps.kH, nullptr, k_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.g.Hn) &&
+         encode_ranks(maps.vH, nullptr, v_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.g.Hn);
+  if (!ok) return SBDA_ERR_UNSUPPORTED;
+  return v1_forward_sharded(dtype, maps, p, pl, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int32_t* offsets,
+                                          int32_t n_offsets, float scale, int32_t rank, int32_t world,
+                                          const sbda_tensor* q_ranks, const sbda_tensor* k_ranks,
+                                          const sbda_tensor* v_ranks, const sbda_tensor* grad_out_ranks,
+                                          const float* const* lse_ranks, sbda_tensor grad_q, sbda_tensor grad_k,
+                                          sbda_tensor grad_v, void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  if (world < 1 || world > kMaxShards || rank < 0 || rank >= world || !q_ranks || !k_ranks || !v_ranks ||
+      !grad_out_ranks || !lse_ranks)
+    return SBDA_ERR_INVALID;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, Ls = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || Ls == 0) return SBDA_OK;
+  if (!grad_q.data || !grad_k.data || !grad_v.data) return SBDA_ERR_INVALID;
+  for (int r = 0; r < world; ++r)
+    if (!q_ranks[r].data || !k_ranks[r].data || !v_ranks[r].data || !grad_out_ranks[r].data || !lse_ranks[r])
+      return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  Plan pl;
+  st = plan_sharded(offsets, n_offsets, Ls, D, e, world, &pl);
+  if (st != SBDA_OK) return st;
+  if (!vector_ok(grad_q, B, H, Ls, D, e) || !vector_ok(grad_k, B, Hkv, Ls, D, e) ||
+      !vector_ok(grad_v, B, Hkv, Ls, D, e))
+    return SBDA_ERR_UNSUPPORTED;
+
+  BwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = (int)B;
+  p.H = (int)H;
+  p.Hkv = (int)Hkv;
+  p.G = (int)(H / Hkv);
+  p.L = (int)Ls;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = pl.g;
+  p.q = arg_of(q_ranks[rank]);
+  p.k = arg_of(k_ranks[rank]);
+  p.v = arg_of(v_ranks[rank]);
+  p.dout = arg_of(grad_out_ranks[rank]);
+  p.dq = arg_of(grad_q);
+  p.dk = arg_of(grad_k);
+  p.dv = arg_of(grad_v);
+  p.lse = lse_ranks[rank];
+  p.status = status_ptr();
+  p.sh = shard_info(rank, world, Ls);
+  for (int r = 0; r < world; ++r) p.sh.lse[r] = lse_ranks[r];
+
+  ShardBwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  bool ok = encode_ranks(maps.qT, &p.slots_q, q_ranks, world, dtype, B, H, Ls, D, pl.pitch, pl.tile) &&
+            encode_ranks(maps.dT, &p.slots_d, grad_out_ranks, world, dtype, B, H, Ls, D, pl.pitch, pl.tile) &&
+            encode_ranks(maps.kT, &p.slots_k, k_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.tile) &&
+            encode_ranks(maps.vT, &p.slots_v, v_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.tile);
+  if (ok && pl.g.Hn > 0)
+    ok = encode_ranks(maps.qH, nullptr, q_ranks, world, dtype, B, H, Ls, D, pl.pitch, pl.g.Hn) &&
+         encode_ranks(maps.dH, nullptr, grad_out_ranks, world, dtype, B, H, Ls, D, pl.pitch, pl.g.Hn) &&
+         encode_ranks(maps.kH, nullptr, k_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.g.Hn) &&
+         encode_ranks(maps.vH, nullptr, v_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.g.Hn);
+  if (!ok) return SBDA_ERR_UNSUPPORTED;
+  return v1_backward_sharded(dtype, maps, p, pl, reinterpret_cast<cudaStream_t>(stream));
 }

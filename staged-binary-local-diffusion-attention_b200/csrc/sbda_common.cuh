@@ -39,6 +39,18 @@ struct Geometry {
   int R, A, rem;   // chain order: R = f / TILE tiles per chain step (0 = linear)
 };
 
+// Contiguous sequence shards: rank r holds positions [r * shard_len,
+// (r + 1) * shard_len) of a sequence of total_len positions.  One GPU is the
+// case world = 1, shard_len = total_len, pos0 = 0.
+constexpr int kMaxShards = 8;
+struct ShardInfo {
+  int rank, world;
+  int shard_len;                 // positions per rank
+  int pos0;                      // global position of local row 0
+  int total_len;                 // positions of the whole sequence
+  const float* lse[kMaxShards];  // per-rank log-sum-exp bases [B, H, shard_len] (backward)
+};
+
 struct FwdParams {
   int B, H, Hkv, G, L, D;
   float scale;
@@ -47,6 +59,7 @@ struct FwdParams {
   float* lse;
   unsigned slots_q, slots_k, slots_v;
   unsigned* status;
+  ShardInfo sh;
 };
 
 struct BwdParams {
@@ -57,6 +70,7 @@ struct BwdParams {
   const float* lse;
   unsigned slots_q, slots_k, slots_v, slots_d;
   unsigned* status;
+  ShardInfo sh;
 };
 
 // Tensor maps: *T = TILE-row box, *H = Hn-row halo box.
@@ -66,6 +80,39 @@ struct FwdMaps {
 struct BwdMaps {
   CUtensorMap qT, qH, dT, dH, kT, kH, vT, vH;
 };
+
+// Sequence-sharded maps: one map per rank over that rank's buffer (peer
+// memory mapped into this process), selected per staged region by its owner.
+struct ShardFwdMaps {
+  CUtensorMap qT, kT[kMaxShards], kH[kMaxShards], vT[kMaxShards], vH[kMaxShards];
+};
+struct ShardBwdMaps {
+  CUtensorMap qT[kMaxShards], qH[kMaxShards], dT[kMaxShards], dH[kMaxShards];
+  CUtensorMap kT[kMaxShards], kH[kMaxShards], vT[kMaxShards], vH[kMaxShards];
+};
+
+// Map and map coordinate of the rows starting at global position gpos.
+// One GPU: the map itself.  Shards: the owning rank's map; positions outside
+// the sequence use this rank's map at an out-of-range coordinate, which the
+// copy engine zero-fills.
+__device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap& m, const ShardInfo& s, int gpos,
+                                                       int& coord) {
+  coord = gpos - s.pos0;
+  return &m;
+}
+__device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap (&m)[kMaxShards], const ShardInfo& s,
+                                                       int gpos, int& coord) {
+  int owner = s.rank;
+  if (gpos >= 0 && gpos < s.total_len) owner = gpos / s.shard_len;
+  coord = gpos - owner * s.shard_len;
+  return &m[owner];
+}
+
+// Log-sum-exp of (b, h) at global position q (0 <= q < total_len).
+__device__ __forceinline__ float lse_at(const ShardInfo& s, long long bh, int q) {
+  const int owner = s.world == 1 ? 0 : q / s.shard_len;
+  return s.lse[owner][bh * s.shard_len + (q - owner * s.shard_len)];
+}
 
 // --------------------------------------------------------------------------
 // Device helpers: mbarrier + TMA (inline PTX), element packing
@@ -486,6 +533,8 @@ struct Plan {
 
 int v1_forward(int dtype, bool tma, const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st);
 int v1_backward(int dtype, bool tma, const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st);
+int v1_forward_sharded(int dtype, const ShardFwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st);
+int v1_backward_sharded(int dtype, const ShardBwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st);
 
 struct V2Plan {
   int lpr;

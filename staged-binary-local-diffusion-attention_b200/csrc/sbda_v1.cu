@@ -29,8 +29,8 @@ namespace sbda {
 // Forward
 // --------------------------------------------------------------------------
 
-template <typename TE, int NV, int TILE, bool TMA>
-__global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constant__ FwdMaps maps,
+template <typename TE, int NV, int TILE, bool TMA, typename Maps = FwdMaps>
+__global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constant__ Maps maps,
                                                             const FwdParams p) {
   constexpr int VE = 16 / sizeof(TE);
   constexpr int EPL = NV * VE;
@@ -46,7 +46,8 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constan
   const int t = chain_tile(bid % g.nT, g);
   const int b = bid / g.nT;
   const int hk = h / p.G;
-  const int i0 = t * TILE;
+  const int i0 = t * TILE;          // local tile start
+  const int i0g = p.sh.pos0 + i0;   // its global position
   const int Hn = g.Hn;
 
   uint8_t* Qs = smem;
@@ -65,16 +66,17 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constan
     if (tid == 0) {
       const uint32_t bytes = (uint32_t)((TILE * (3 + 2 * g.has_far) + 2 * Hn) * P);
       mbar_arrive_expect_tx(bar, bytes);
+      int c;
       tma_rows(Qs, &maps.qT, bar, p.slots_q, i0, h, b);
       if (Hn > 0) {
-        tma_rows(Kn, &maps.kH, bar, p.slots_k, i0 - Hn, hk, b);
-        tma_rows(Vn, &maps.vH, bar, p.slots_v, i0 - Hn, hk, b);
+        tma_rows(Kn, pick_map(maps.kH, p.sh, i0g - Hn, c), bar, p.slots_k, c, hk, b);
+        tma_rows(Vn, pick_map(maps.vH, p.sh, i0g - Hn, c), bar, p.slots_v, c, hk, b);
       }
-      tma_rows(Kn + Hn * P, &maps.kT, bar, p.slots_k, i0, hk, b);
-      tma_rows(Vn + Hn * P, &maps.vT, bar, p.slots_v, i0, hk, b);
+      tma_rows(Kn + Hn * P, pick_map(maps.kT, p.sh, i0g, c), bar, p.slots_k, c, hk, b);
+      tma_rows(Vn + Hn * P, pick_map(maps.vT, p.sh, i0g, c), bar, p.slots_v, c, hk, b);
       if (g.has_far) {
-        tma_rows(Kf, &maps.kT, bar, p.slots_k, i0 - g.f, hk, b);
-        tma_rows(Vf, &maps.vT, bar, p.slots_v, i0 - g.f, hk, b);
+        tma_rows(Kf, pick_map(maps.kT, p.sh, i0g - g.f, c), bar, p.slots_k, c, hk, b);
+        tma_rows(Vf, pick_map(maps.vT, p.sh, i0g - g.f, c), bar, p.slots_v, c, hk, b);
       }
     }
     const bool ok = mbar_wait_bounded(bar, 0);
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constan
   float* lse = p.lse + ((long long)b * p.H + h) * p.L;
 #pragma unroll 1
   for (int r = grp; r < TILE; r += kGroups) {
-    const int i = i0 + r;
+    const int i = i0g + r;  // global position (masks); stores use the local row i0 + r
     float qf[EPL];
     load_row<TE, NV>(Qs + r * P, l8, qf);
     float sc[4];
@@ -142,10 +144,11 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constan
         for (int e = 0; e < EPL; ++e) of[e] = fmaf(w, vf[e], of[e]);
       }
     }
-    if (i < p.L) {
-      TE* orow = out + (long long)b * p.out.sb + (long long)h * p.out.sh + (long long)i * p.out.sl;
+    const int il = i0 + r;
+    if (il < p.L) {
+      TE* orow = out + (long long)b * p.out.sb + (long long)h * p.out.sh + (long long)il * p.out.sl;
       store_row<TE, NV, TMA>(orow, p.out.sd, p.D, l8, of);
-      if (l8 == 0) lse[i] = sum > 0.f ? mx + __logf(sum) : -INFINITY;
+      if (l8 == 0) lse[il] = sum > 0.f ? mx + __logf(sum) : -INFINITY;
     }
   }
 }
@@ -154,8 +157,8 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_kernel(const __grid_constan
 // Backward (gather form)
 // --------------------------------------------------------------------------
 
-template <typename TE, int NV, int TILE, bool TMA>
-__global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constant__ BwdMaps maps,
+template <typename TE, int NV, int TILE, bool TMA, typename Maps = BwdMaps>
+__global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constant__ Maps maps,
                                                             const BwdParams p) {
   constexpr int VE = 16 / sizeof(TE);
   constexpr int EPL = NV * VE;
@@ -171,7 +174,8 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constan
   bid /= p.Hkv;
   const int t = chain_tile(bid % g.nT, g);
   const int b = bid / g.nT;
-  const int j0 = t * TILE;
+  const int j0 = t * TILE;          // local tile start
+  const int j0g = p.sh.pos0 + j0;   // its global position
   const int Hn = g.Hn, far = g.has_far, f = g.f;
   const int NC = TILE + Hn + (far ? TILE : 0);  // consumer rows
 
@@ -214,35 +218,36 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constan
         uint32_t rows = 2 * (TILE + Hn) + (far ? 2 * TILE : 0);
         if (gi == 0) rows += 2 * (TILE + 2 * Hn) + (far ? 2 * (TILE + Hn) + 2 * (Hn + TILE) : 0);
         mbar_arrive_expect_tx(bar, rows * P);
-        tma_rows(QN, &maps.qT, bar, p.slots_q, j0, h, b);
-        tma_rows(DN, &maps.dT, bar, p.slots_d, j0, h, b);
+        int c;
+        tma_rows(QN, pick_map(maps.qT, p.sh, j0g, c), bar, p.slots_q, c, h, b);
+        tma_rows(DN, pick_map(maps.dT, p.sh, j0g, c), bar, p.slots_d, c, h, b);
         if (Hn > 0) {
-          tma_rows(QN + TILE * P, &maps.qH, bar, p.slots_q, j0 + TILE, h, b);
-          tma_rows(DN + TILE * P, &maps.dH, bar, p.slots_d, j0 + TILE, h, b);
+          tma_rows(QN + TILE * P, pick_map(maps.qH, p.sh, j0g + TILE, c), bar, p.slots_q, c, h, b);
+          tma_rows(DN + TILE * P, pick_map(maps.dH, p.sh, j0g + TILE, c), bar, p.slots_d, c, h, b);
         }
         if (far) {
-          tma_rows(QF, &maps.qT, bar, p.slots_q, j0 + f, h, b);
-          tma_rows(DF, &maps.dT, bar, p.slots_d, j0 + f, h, b);
+          tma_rows(QF, pick_map(maps.qT, p.sh, j0g + f, c), bar, p.slots_q, c, h, b);
+          tma_rows(DF, pick_map(maps.dT, p.sh, j0g + f, c), bar, p.slots_d, c, h, b);
         }
         if (gi == 0) {
-          tma_rows(KN + Hn * P, &maps.kT, bar, p.slots_k, j0, hk, b);
-          tma_rows(VN + Hn * P, &maps.vT, bar, p.slots_v, j0, hk, b);
+          tma_rows(KN + Hn * P, pick_map(maps.kT, p.sh, j0g, c), bar, p.slots_k, c, hk, b);
+          tma_rows(VN + Hn * P, pick_map(maps.vT, p.sh, j0g, c), bar, p.slots_v, c, hk, b);
           if (Hn > 0) {
-            tma_rows(KN, &maps.kH, bar, p.slots_k, j0 - Hn, hk, b);
-            tma_rows(VN, &maps.vH, bar, p.slots_v, j0 - Hn, hk, b);
-            tma_rows(KN + (Hn + TILE) * P, &maps.kH, bar, p.slots_k, j0 + TILE, hk, b);
-            tma_rows(VN + (Hn + TILE) * P, &maps.vH, bar, p.slots_v, j0 + TILE, hk, b);
+            tma_rows(KN, pick_map(maps.kH, p.sh, j0g - Hn, c), bar, p.slots_k, c, hk, b);
+            tma_rows(VN, pick_map(maps.vH, p.sh, j0g - Hn, c), bar, p.slots_v, c, hk, b);
+            tma_rows(KN + (Hn + TILE) * P, pick_map(maps.kH, p.sh, j0g + TILE, c), bar, p.slots_k, c, hk, b);
+            tma_rows(VN + (Hn + TILE) * P, pick_map(maps.vH, p.sh, j0g + TILE, c), bar, p.slots_v, c, hk, b);
           }
           if (far) {
-            tma_rows(KFL, &maps.kT, bar, p.slots_k, j0 - f, hk, b);
-            tma_rows(VFL, &maps.vT, bar, p.slots_v, j0 - f, hk, b);
-            tma_rows(KFR + Hn * P, &maps.kT, bar, p.slots_k, j0 + f, hk, b);
-            tma_rows(VFR + Hn * P, &maps.vT, bar, p.slots_v, j0 + f, hk, b);
+            tma_rows(KFL, pick_map(maps.kT, p.sh, j0g - f, c), bar, p.slots_k, c, hk, b);
+            tma_rows(VFL, pick_map(maps.vT, p.sh, j0g - f, c), bar, p.slots_v, c, hk, b);
+            tma_rows(KFR + Hn * P, pick_map(maps.kT, p.sh, j0g + f, c), bar, p.slots_k, c, hk, b);
+            tma_rows(VFR + Hn * P, pick_map(maps.vT, p.sh, j0g + f, c), bar, p.slots_v, c, hk, b);
             if (Hn > 0) {
-              tma_rows(KFL + TILE * P, &maps.kH, bar, p.slots_k, j0 - f + TILE, hk, b);
-              tma_rows(VFL + TILE * P, &maps.vH, bar, p.slots_v, j0 - f + TILE, hk, b);
-              tma_rows(KFR, &maps.kH, bar, p.slots_k, j0 + f - Hn, hk, b);
-              tma_rows(VFR, &maps.vH, bar, p.slots_v, j0 + f - Hn, hk, b);
+              tma_rows(KFL + TILE * P, pick_map(maps.kH, p.sh, j0g - f + TILE, c), bar, p.slots_k, c, hk, b);
+              tma_rows(VFL + TILE * P, pick_map(maps.vH, p.sh, j0g - f + TILE, c), bar, p.slots_v, c, hk, b);
+              tma_rows(KFR, pick_map(maps.kH, p.sh, j0g + f - Hn, c), bar, p.slots_k, c, hk, b);
+              tma_rows(VFR, pick_map(maps.vH, p.sh, j0g + f - Hn, c), bar, p.slots_v, c, hk, b);
             }
           }
         }
@@ -274,16 +279,16 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constan
     }
 
     // ---- Phase 1: softmax of every consumer query; dQ of own queries. ----
-    const float* lse = p.lse + ((long long)b * p.H + h) * p.L;
+    const long long bh = (long long)b * p.H + h;
 #pragma unroll 1
     for (int base = 0; base < NC; base += kGroups) {
       const bool act = base + grp < NC;
       const int c = act ? base + grp : NC - 1;
       const bool nearc = c < TILE + Hn;
       const int cf = c - (TILE + Hn);
-      const int q = nearc ? j0 + c : j0 + f + cf;
-      const bool inr = q < p.L;
-      const float lq = inr ? lse[q] : 0.f;
+      const int q = nearc ? j0g + c : j0g + f + cf;  // global consumer position
+      const bool inr = q < p.sh.total_len;
+      const float lq = inr ? lse_at(p.sh, bh, q) : 0.f;
       float qf[EPL], df[EPL];
       load_row<TE, NV>(nearc ? QN + c * P : QF + cf * P, l8, qf);
       load_row<TE, NV>(nearc ? DN + c * P : DF + cf * P, l8, df);
@@ -335,7 +340,7 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constan
             for (int e = 0; e < EPL; ++e) gq[e] = fmaf(w, kf[e], gq[e]);
           }
         }
-        TE* dst = dq_base + (long long)b * p.dq.sb + (long long)h * p.dq.sh + (long long)q * p.dq.sl;
+        TE* dst = dq_base + (long long)b * p.dq.sb + (long long)h * p.dq.sh + (long long)(j0 + c) * p.dq.sl;
         store_row<TE, NV, TMA>(dst, p.dq.sd, p.D, l8, gq);
       }
       if (act && l8 < 4) {
@@ -394,9 +399,9 @@ __global__ void __launch_bounds__(kThreads) sbda_bwd_kernel(const __grid_constan
   }
 }
 
-template <typename TE, int NV, int TILE, bool TMA>
-int launch_fwd(const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t stream) {
-  auto kern = sbda_fwd_kernel<TE, NV, TILE, TMA>;
+template <typename TE, int NV, int TILE, bool TMA, typename Maps = FwdMaps>
+int launch_fwd(const Maps& maps, const FwdParams& p, const Plan& pl, cudaStream_t stream) {
+  auto kern = sbda_fwd_kernel<TE, NV, TILE, TMA, Maps>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_fwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
   const long long blocks = (long long)p.B * p.H * pl.g.nT;
@@ -404,9 +409,9 @@ int launch_fwd(const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStre
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
-template <typename TE, int NV, int TILE, bool TMA>
-int launch_bwd(const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t stream) {
-  auto kern = sbda_bwd_kernel<TE, NV, TILE, TMA>;
+template <typename TE, int NV, int TILE, bool TMA, typename Maps = BwdMaps>
+int launch_bwd(const Maps& maps, const BwdParams& p, const Plan& pl, cudaStream_t stream) {
+  auto kern = sbda_bwd_kernel<TE, NV, TILE, TMA, Maps>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
   const long long blocks = (long long)p.B * p.Hkv * pl.g.nT;
@@ -415,45 +420,57 @@ int launch_bwd(const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStre
 }
 
 // Instantiated (pitch, tile) pairs: 128 B -> 64; 256 B -> 64, 32; 512 B -> 32, 16.
-#define SBDA_FOR_TILES(LAUNCH, TE, TMA, ...)                                        \
-  do {                                                                              \
-    if (pl.nv == 1 && pl.tile == 64) return LAUNCH<TE, 1, 64, TMA>(__VA_ARGS__);    \
-    if (pl.nv == 2 && pl.tile == 64) return LAUNCH<TE, 2, 64, TMA>(__VA_ARGS__);    \
-    if (pl.nv == 2 && pl.tile == 32) return LAUNCH<TE, 2, 32, TMA>(__VA_ARGS__);    \
-    if (pl.nv == 4 && pl.tile == 32) return LAUNCH<TE, 4, 32, TMA>(__VA_ARGS__);    \
-    if (pl.nv == 4 && pl.tile == 16) return LAUNCH<TE, 4, 16, TMA>(__VA_ARGS__);    \
-    return SBDA_ERR_UNSUPPORTED;                                                    \
+#define SBDA_FOR_TILES(LAUNCH, TE, TMA, MAPS, ...)                                        \
+  do {                                                                                   \
+    if (pl.nv == 1 && pl.tile == 64) return LAUNCH<TE, 1, 64, TMA, MAPS>(__VA_ARGS__);   \
+    if (pl.nv == 2 && pl.tile == 64) return LAUNCH<TE, 2, 64, TMA, MAPS>(__VA_ARGS__);   \
+    if (pl.nv == 2 && pl.tile == 32) return LAUNCH<TE, 2, 32, TMA, MAPS>(__VA_ARGS__);   \
+    if (pl.nv == 4 && pl.tile == 32) return LAUNCH<TE, 4, 32, TMA, MAPS>(__VA_ARGS__);   \
+    if (pl.nv == 4 && pl.tile == 16) return LAUNCH<TE, 4, 16, TMA, MAPS>(__VA_ARGS__);   \
+    return SBDA_ERR_UNSUPPORTED;                                                         \
   } while (0)
 
-template <typename TE, bool TMA>
-int fwd_tiles(const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st) {
-  SBDA_FOR_TILES(launch_fwd, TE, TMA, maps, p, pl, st);
+template <typename TE, bool TMA, typename Maps>
+int fwd_tiles(const Maps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st) {
+  SBDA_FOR_TILES(launch_fwd, TE, TMA, Maps, maps, p, pl, st);
 }
-template <typename TE, bool TMA>
-int bwd_tiles(const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st) {
-  SBDA_FOR_TILES(launch_bwd, TE, TMA, maps, p, pl, st);
-}
-
-template <bool TMA>
-int fwd_dtype_v1(int dtype, const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st) {
-  if (dtype == SBDA_DTYPE_F32) return fwd_tiles<float, TMA>(maps, p, pl, st);
-  if (dtype == SBDA_DTYPE_F16) return fwd_tiles<__half, TMA>(maps, p, pl, st);
-  return fwd_tiles<__nv_bfloat16, TMA>(maps, p, pl, st);
-}
-template <bool TMA>
-int bwd_dtype_v1(int dtype, const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st) {
-  if (dtype == SBDA_DTYPE_F32) return bwd_tiles<float, TMA>(maps, p, pl, st);
-  if (dtype == SBDA_DTYPE_F16) return bwd_tiles<__half, TMA>(maps, p, pl, st);
-  return bwd_tiles<__nv_bfloat16, TMA>(maps, p, pl, st);
+template <typename TE, bool TMA, typename Maps>
+int bwd_tiles(const Maps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st) {
+  SBDA_FOR_TILES(launch_bwd, TE, TMA, Maps, maps, p, pl, st);
 }
 
+template <bool TMA, typename Maps>
+int fwd_dtype_v1(int dtype, const Maps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st) {
+  if (dtype == SBDA_DTYPE_F32) return fwd_tiles<float, TMA, Maps>(maps, p, pl, st);
+  if (dtype == SBDA_DTYPE_F16) return fwd_tiles<__half, TMA, Maps>(maps, p, pl, st);
+  return fwd_tiles<__nv_bfloat16, TMA, Maps>(maps, p, pl, st);
+}
+template <bool TMA, typename Maps>
+int bwd_dtype_v1(int dtype, const Maps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st) {
+  if (dtype == SBDA_DTYPE_F32) return bwd_tiles<float, TMA, Maps>(maps, p, pl, st);
+  if (dtype == SBDA_DTYPE_F16) return bwd_tiles<__half, TMA, Maps>(maps, p, pl, st);
+  return bwd_tiles<__nv_bfloat16, TMA, Maps>(maps, p, pl, st);
+}
 
 int v1_forward(int dtype, bool tma, const FwdMaps& maps, const FwdParams& p, const Plan& pl, cudaStream_t st) {
-  return tma ? fwd_dtype_v1<true>(dtype, maps, p, pl, st) : fwd_dtype_v1<false>(dtype, maps, p, pl, st);
+  return tma ? fwd_dtype_v1<true, FwdMaps>(dtype, maps, p, pl, st)
+             : fwd_dtype_v1<false, FwdMaps>(dtype, maps, p, pl, st);
 }
 
 int v1_backward(int dtype, bool tma, const BwdMaps& maps, const BwdParams& p, const Plan& pl, cudaStream_t st) {
-  return tma ? bwd_dtype_v1<true>(dtype, maps, p, pl, st) : bwd_dtype_v1<false>(dtype, maps, p, pl, st);
+  return tma ? bwd_dtype_v1<true, BwdMaps>(dtype, maps, p, pl, st)
+             : bwd_dtype_v1<false, BwdMaps>(dtype, maps, p, pl, st);
+}
+
+// Sequence-sharded: the copy-engine path only (peer buffers are staged by TMA).
+int v1_forward_sharded(int dtype, const ShardFwdMaps& maps, const FwdParams& p, const Plan& pl,
+                       cudaStream_t st) {
+  return fwd_dtype_v1<true, ShardFwdMaps>(dtype, maps, p, pl, st);
+}
+
+int v1_backward_sharded(int dtype, const ShardBwdMaps& maps, const BwdParams& p, const Plan& pl,
+                        cudaStream_t st) {
+  return bwd_dtype_v1<true, ShardBwdMaps>(dtype, maps, p, pl, st);
 }
 
 }  // namespace sbda

@@ -1,0 +1,64 @@
+"""Host-side shard arithmetic on two gloo ranks (no GPU): shards partition the sequence and
+every rank agrees on the owner of every position, including the dyadic sources and consumers
+the sharded kernels fetch from other ranks."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from sbda_b200.sharded import owner_of, shard_bounds
+
+TOTAL = 4096
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lo, hi = shard_bounds(TOTAL, world, rank)
+        bounds = [None] * world
+        dist.all_gather_object(bounds, (lo, hi))
+        assert bounds[0][0] == 0 and bounds[-1][1] == TOTAL
+        assert all(bounds[i][1] == bounds[i + 1][0] for i in range(world - 1))
+        # every rank computes the owner of its rows' dyadic sources/consumers; all must agree
+        mine = {}
+        for d in (1, 2, 64, 256, TOTAL // world, TOTAL // 2):
+            for pos in (lo, lo + 1, hi - 1):
+                for other in (pos - d, pos + d):
+                    if 0 <= other < TOTAL:
+                        mine[(pos, other)] = owner_of(other, TOTAL, world)
+        views = [None] * world
+        dist.all_gather_object(views, mine)
+        merged = {}
+        for view in views:
+            for key, owner in view.items():
+                assert merged.setdefault(key, owner) == owner
+                lo_o, hi_o = bounds[owner]
+                assert lo_o <= key[1] < hi_o
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_shard_plan_agrees():
+    mp.spawn(_worker, args=(2, _port()), nprocs=2, join=True)
+
+
+def test_shard_bounds_validation():
+    import pytest
+
+    with pytest.raises(ValueError):
+        shard_bounds(10, 3, 0)
+    with pytest.raises(ValueError):
+        owner_of(10, 10, 2)
+    assert torch.tensor([shard_bounds(8, 4, r)[0] for r in range(4)]).tolist() == [0, 2, 4, 6]
