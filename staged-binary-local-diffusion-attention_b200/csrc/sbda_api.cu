@@ -136,6 +136,20 @@ bool encode_map(CUtensorMap* map, unsigned* slots, const sbda_tensor& t, int dty
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over the fp32 log-sum-exp rows [rows, L] (contiguous); needs the
+// row stride L * 4 to be a multiple of 16 bytes.
+bool encode_lse_map(CUtensorMap* map, const float* lse, int64_t rows, int64_t L, int box) {
+  auto enc = encode_fn();
+  if (!enc || L % 4 || reinterpret_cast<uintptr_t>(lse) % 16) return false;
+  cuuint64_t gdim[2] = {(cuuint64_t)L, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)(L * 4)};
+  cuuint32_t boxd[2] = {(cuuint32_t)box, 1};
+  cuuint32_t estride[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(lse), gdim, gstride, boxd, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Splits offsets into the near window and at most one far offset for a tile
 // height, and sizes the staged regions.  Returns false when the offsets need
 // two far tiles at this tile height.
@@ -252,7 +266,8 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   pl->pitch = pitch;
   pl->smem_fwd = (Tz + 2 * (Tz + 2) + 2 * Tz * g.has_far) * P + 16;
   const size_t nkv = g.mode == 0 ? 2 : 1, kvr = Tz + 2 * hz, qdr = Tz + hz;
-  pl->smem_bwd = nkv * 2 * kvr * P + 2 * 2 * qdr * P + qdr * 4 * sizeof(float2) + 16;
+  pl->lse_box = (int)((qdr + 31) / 32 * 32);  // fp32 rows; 128-byte multiples
+  pl->smem_bwd = nkv * 2 * kvr * P + 2 * 2 * qdr * P + qdr * 4 * sizeof(float2) + 128 + 2 * pl->lse_box * 4 + 16;
   if (pl->smem_fwd > kMaxSmem || pl->smem_bwd > kMaxSmem) return false;
   // Backward work split: about four CTAs' worth of tiles per resident slot.
   const int64_t total = B * H * (int64_t)g.nT;
@@ -456,6 +471,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
     BwdMaps maps;
     memset(&maps, 0, sizeof(maps));
     bool tma = vec;
+    p.lse_box = p2.lse_box;
     if (tma) {
       unsigned dummy;
       const int hz = p2.g.halo;
@@ -467,6 +483,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
             encode_map(&maps.dH, &dummy, grad_out, dtype, B, H, L, D, p2.pitch, hz) &&
             encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, hz) &&
             encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, hz);
+      p.lse_tma = tma && encode_lse_map(&maps.lseT, lse, B * H, L, p2.lse_box);
     }
     return v2_backward(dtype, tma, maps, p, p2, s);
   }

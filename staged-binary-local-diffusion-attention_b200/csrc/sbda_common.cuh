@@ -79,6 +79,7 @@ struct FwdMaps {
 };
 struct BwdMaps {
   CUtensorMap qT, qH, dT, dH, kT, kH, vT, vH;
+  CUtensorMap lseT;  // windowed backward: fp32 [B*H, L] rows, box of the Q/dO slot height (rounded to 32)
 };
 
 // Sequence-sharded maps: one map per rank over that rank's buffer (peer
@@ -185,6 +186,16 @@ __device__ __forceinline__ void tma_rows(void* dst, const CUtensorMap* map, uint
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// 2-D tiled TMA load (fp32 LSE rows): coordinate 0 = position (a multiple of
+// 4, so the 16-byte rule on the innermost coordinate holds), 1 = batch*head.
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
 
@@ -516,6 +527,8 @@ struct BwdV2Params {
   const float* lse;
   unsigned slots_q, slots_k, slots_v, slots_d;
   unsigned* status;
+  int lse_tma;   // 1: LSE rows staged by the copy engine with Q/dO (L % 4 == 0)
+  int lse_box;   // rows of that box (Q/dO slot height rounded up to 32)
 };
 
 // v2 tile height for a row pitch: each of the 128/LPR row groups owns a run of
@@ -540,6 +553,7 @@ struct V2Plan {
   int lpr;
   int tile;
   int pitch;
+  int lse_box;
   V2Geometry g;
   size_t smem_fwd, smem_bwd;
   unsigned blocks_bwd;

@@ -260,7 +260,9 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
   uint8_t* QDbase = KVbase + nkv * 2 * KVR * P;  // 2 slots of [Q rows][dO rows]
   // Per consumer: (p0, ds0, p1, ds1) (p2, ds2, pf, dsf); ds already scaled by head_dim^-0.5.
   float4* E = reinterpret_cast<float4*>(QDbase + 2 * 2 * QDR * P);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(E + QDR * 2);
+  // Two LSE slots of lse_box fp32 rows each (128-byte multiples), 128-byte aligned after E.
+  float* LSEs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(E + QDR * 2) + 127) & ~uintptr_t(127));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(LSEs + 2 * p.lse_box);
   auto kslot = [&](int s) { return KVbase + s * 2 * KVR * P; };
   auto vslot = [&](int s) { return KVbase + s * 2 * KVR * P + KVR * P; };
   auto qslot = [&](int s) { return QDbase + s * 2 * QDR * P; };
@@ -273,8 +275,9 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     const int j0 = (t_first - i * stride) * T;
     if constexpr (TMA) {
       uint64_t* bar = bars + (i & 1);
-      mbar_arrive_expect_tx(bar, (uint32_t)(2 * QDR * P));
+      mbar_arrive_expect_tx(bar, (uint32_t)(2 * QDR * P + (p.lse_tma ? p.lse_box * 4 : 0)));
       tma_qd_slot<TE, T, P>(maps, p, bar, qslot(i & 1), dslot(i & 1), j0, Hc, h, b);
+      if (p.lse_tma) tma_2d(LSEs + (i & 1) * p.lse_box, &maps.lseT, bar, j0, b * p.H + h);
     } else {
       constexpr int PE = P / sizeof(TE);
       generic_rows<TE>(qslot(i & 1), p.q, b, h, j0, QDR, p.L, p.D, PE);
@@ -408,7 +411,9 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
       const int a = grp * 4;
       float lq[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) lq[i] = (j0 + a + i < p.L) ? lse[j0 + a + i] * kLog2e : 0.f;
+      const float* ls = LSEs + (step & 1) * p.lse_box;
+      for (int i = 0; i < 4; ++i)
+        lq[i] = (TMA && p.lse_tma) ? ls[a + i] * kLog2e : ((j0 + a + i < p.L) ? lse[j0 + a + i] * kLog2e : 0.f);
       Frag k1 = FragIO<TE>::load(KN + (a + Hc - 1) * P, l), k2 = FragIO<TE>::load(KN + (a + Hc - 2) * P, l);
       Frag v1 = FragIO<TE>::load(VN + (a + Hc - 1) * P, l), v2 = FragIO<TE>::load(VN + (a + Hc - 2) * P, l);
 #pragma unroll
@@ -438,7 +443,8 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
         for (int i = 0; i < xr; ++i) {
           const bool act = e0 + i < Hc;
           const int c = act ? T + e0 + i : cbase;
-          const float lq = (act && j0 + c < p.L) ? lse[j0 + c] * kLog2e : 0.f;
+          const float lq = (TMA && p.lse_tma) ? LSEs[(step & 1) * p.lse_box + c] * kLog2e
+                                              : ((act && j0 + c < p.L) ? lse[j0 + c] * kLog2e : 0.f);
           const Frag k0 = FragIO<TE>::load(KN + (c + Hc) * P, l);
           const Frag v0 = FragIO<TE>::load(VN + (c + Hc) * P, l);
           consume(c, act, k0, v0, k1, v1, k2, v2, lq);
