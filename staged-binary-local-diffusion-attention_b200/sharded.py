@@ -43,15 +43,20 @@ def owner_of(position: int, total_len: int, world: int) -> int:
 
 
 class ShardGroup:
-    """Symmetric buffers and peer addresses for one process group."""
+    """Symmetric buffers and peer addresses for one process group.
+
+    Without an initialised process group it is a one-rank group on the current GPU (ordinary
+    memory, no barrier), so the same code runs on one GPU.
+    """
 
     def __init__(self, group: dist.ProcessGroup | None = None) -> None:
         import torch.distributed._symmetric_memory as symm_mem
 
         self._symm = symm_mem
-        self.group = group if group is not None else dist.group.WORLD
-        self.rank = dist.get_rank(self.group)
-        self.world = dist.get_world_size(self.group)
+        self.single = group is None and not (dist.is_available() and dist.is_initialized())
+        self.group = None if self.single else (group if group is not None else dist.group.WORLD)
+        self.rank = 0 if self.single else dist.get_rank(self.group)
+        self.world = 1 if self.single else dist.get_world_size(self.group)
         if self.world > 8:
             raise ValueError("at most 8 sequence shards")
         self._handles: dict[int, tuple[object, int]] = {}
@@ -60,6 +65,8 @@ class ShardGroup:
     def empty(self, *shape: int, dtype: torch.dtype, device: torch.device | None = None) -> Tensor:
         """A tensor every rank of the group can read (collective: all ranks call it alike)."""
         device = device or torch.device("cuda", torch.cuda.current_device())
+        if self.single:  # one GPU, no process group: ordinary memory, no peers
+            return torch.empty(*shape, dtype=dtype, device=device)
         t = self._symm.empty(*shape, dtype=dtype, device=device)
         handle = self._symm.rendezvous(t, self.group)
         self._handles[t.untyped_storage().data_ptr()] = (handle, t.untyped_storage().data_ptr())
@@ -69,6 +76,8 @@ class ShardGroup:
 
     def peer_pointers(self, t: Tensor) -> list[int]:
         """``t``'s address on every rank, as pointers valid in this process."""
+        if self.single:
+            return [t.data_ptr()]
         entry = self._handles.get(t.untyped_storage().data_ptr())
         if entry is None:
             raise ValueError("tensor was not allocated by this ShardGroup")
@@ -80,6 +89,8 @@ class ShardGroup:
         """Device-side barrier on the current stream: earlier writes on every rank are visible
         after it.  The wait is bounded (``timeout_ms``), so a rank that never arrives ends the
         wait with an error instead of holding the GPU."""
+        if self.single:
+            return
         if self._barrier_handle is None:
             raise RuntimeError("no symmetric buffer allocated yet")
         self._barrier_handle.barrier(channel=0, timeout_ms=int(timeout_ms))
