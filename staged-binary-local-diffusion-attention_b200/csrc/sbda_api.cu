@@ -223,6 +223,23 @@ int make_plan(const int32_t* off, int n, int64_t L, int64_t D, int e, Plan* pl) 
 // Plan of the windowed kernels (sbda_v2.cu).  They serve MHA schedules whose
 // near offsets lie in {0, 1, 2} with at most one far offset d > 2; the
 // backward walks chains when d is a multiple of the tile height.
+// LSE rows staged per backward step: the Q/dO slot height rounded up to 32
+// (fp32 rows; 128-byte multiples).
+int lse_box_rows(const V2Geometry& g, int T) { return (T + g.halo + 31) / 32 * 32; }
+
+// Dynamic shared memory of the windowed backward for a geometry: K/V slots,
+// two Q/dO slots, the softmax-record ring, two LSE slots and the barriers.
+size_t bwd_smem(const V2Geometry& g, int T, int pitch) {
+  const size_t P = pitch, Tz = T, hz = g.halo;
+  const size_t nkv = g.mode == 0 ? 2 : 1, kvr = g.mode == 2 ? Tz + g.d : Tz + 2 * hz, qdr = Tz + hz;
+  return nkv * 2 * kvr * P + 2 * 2 * qdr * P + v2_ring_floats(T) * sizeof(float) + 128 +
+         2 * (size_t)lse_box_rows(g, T) * 4 + 16;
+}
+
+// Largest per-CTA dynamic shared memory that still lets three CTAs share an
+// SM (228 KB per SM, 1 KB reserved per CTA).
+constexpr size_t kSmemThreeCtas = 228 * 1024 / 3 - 1024;
+
 bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, int64_t B, int64_t H,
              V2Plan* pl) {
   if (G != 1) return false;
@@ -259,23 +276,29 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   } else {
     g.mode = 1;
     g.halo = g.has_far ? (g.d > 2 ? g.d : 2) : 2;
+    // Local mode stages T + 2d K/V rows and T + d Q/dO rows.  When that keeps
+    // fewer than three CTAs on an SM, the local carry walk (T + d and T + 2
+    // rows) serves d % 4 == 0 instead.
+    if (g.has_far && g.d % 4 == 0 && bwd_smem(g, T, pitch) > kSmemThreeCtas) {
+      g.mode = 2;
+      g.halo = 2;
+    }
   }
-  const size_t P = pitch, Tz = T, hz = g.halo;
   pl->lpr = lpr;
   pl->tile = T;
   pl->pitch = pitch;
-  pl->smem_fwd = (Tz + 2 * (Tz + 2) + 2 * Tz * g.has_far) * P + 16;
-  const size_t nkv = g.mode == 0 ? 2 : 1, kvr = Tz + 2 * hz, qdr = Tz + hz;
-  pl->lse_box = (int)((qdr + 31) / 32 * 32);  // fp32 rows; 128-byte multiples
-  pl->smem_bwd = nkv * 2 * kvr * P + 2 * 2 * qdr * P + qdr * 4 * sizeof(float2) + 128 + 2 * pl->lse_box * 4 + 16;
+  pl->smem_fwd = (size_t)(T + 2 * (T + 2) + 2 * T * g.has_far) * pitch + 16;
+  pl->lse_box = lse_box_rows(g, T);
+  pl->smem_bwd = bwd_smem(g, T, pitch);
   if (pl->smem_fwd > kMaxSmem || pl->smem_bwd > kMaxSmem) return false;
   // Backward work split: about four CTAs' worth of tiles per resident slot.
   const int64_t total = B * H * (int64_t)g.nT;
   const int64_t target = (int64_t)sm_count() * 3 * 4;
   int seg = (int)((total + target - 1) / target);
   if (seg < 1) seg = 1;
+  // Chain and local-carry walks open with a carry-only tile: at least four tiles per walk.
+  if (g.mode != 1 && seg < 4) seg = 4;
   if (g.mode == 0) {
-    if (seg < 4) seg = 4;  // amortise the carry-only first tile of a segment
     if (seg >= g.A) seg = g.A;
     g.seg = seg;
     g.segs = (g.A + seg - 1) / seg;
@@ -475,14 +498,15 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
     if (tma) {
       unsigned dummy;
       const int hz = p2.g.halo;
+      const int lead = p2.g.mode == 2 ? p2.g.d : hz;  // K/V rows staged before a tile
       tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p2.pitch, p2.tile) &&
             encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p2.pitch, p2.tile) &&
             encode_map(&maps.kT, &p.slots_k, k, dtype, B, H, L, D, p2.pitch, p2.tile) &&
             encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
             encode_map(&maps.qH, &dummy, q, dtype, B, H, L, D, p2.pitch, hz) &&
             encode_map(&maps.dH, &dummy, grad_out, dtype, B, H, L, D, p2.pitch, hz) &&
-            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, hz) &&
-            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, hz);
+            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, lead) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, lead);
       p.lse_tma = tma && encode_lse_map(&maps.lseT, lse, B * H, L, p2.lse_box);
     }
     return v2_backward(dtype, tma, maps, p, p2, s);

@@ -503,7 +503,8 @@ struct V2Geometry {
   int has_far, d;        // far source: offset d > 2
   int nT;                // tiles per (batch, head)
   int R, A, rem;         // chain order of tiles (forward launch order)
-  int mode;              // backward: 0 = chain walk (d % TILE == 0, d >= TILE), 1 = local tiles
+  int mode;              // backward: 0 = chain walk (d % TILE == 0, d >= TILE), 1 = local tiles,
+                         // 2 = local carry (far d < TILE, d % 4 == 0)
   int halo;              // backward: consumer halo rows past the tile (2, or d in mode 1)
   int seg;               // backward: tiles per CTA
   int segs;              // backward: segments per chain (mode 0) or per (b, h) (mode 1)
@@ -534,6 +535,10 @@ struct BwdV2Params {
 // v2 tile height for a row pitch: each of the 128/LPR row groups owns a run of
 // four consecutive rows.
 __host__ __device__ constexpr int v2_tile(int lpr) { return 4 * (kThreads / lpr); }
+
+// Floats of the backward's softmax-record ring for tile height T: 2T records of
+// 8 floats plus 4 floats of padding per 4 records.
+__host__ __device__ constexpr int v2_ring_floats(int T) { return 2 * T * 8 + (2 * T / 4) * 4; }
 
 // Host-side launchers (defined in sbda_v1.cu / sbda_v2.cu).
 struct Plan {

@@ -21,8 +21,22 @@
 //    alternate: phase 2 (the key gather) reads no K/V, so the next step's far
 //    tile is fetched into this step's near slot as soon as phase 1 is done;
 //    Q/dO are double-buffered and fetched a whole step ahead.
-//  * For d < TILE ("local" mode) a tile also recomputes the d consumers past
-//    its end, which are the far consumers of its last d keys.
+//  * For d < TILE with d % 4 == 0 whose local staging (below) would keep fewer
+//    than three CTAs on an SM ("local carry" mode) a CTA walks consecutive
+//    tiles downwards.  In the key gather, row group g takes keys
+//    4g - d .. 4g - d + 3 (mod TILE), so the far consumer of each of its keys
+//    is one of its own rows 4g .. 4g + 3: in this tile, or (for the last d
+//    keys) in the tile of the step before, whose contribution the same lanes
+//    carried in registers.  No consumer is computed twice except one carry-only
+//    "pre" tile per CTA segment.
+//  * Other d < TILE ("local" mode): the keys of a tile also need the d
+//    consumers past its end, recomputed by the first step of a walk; later
+//    steps take them from the step before (next point).
+//  * The softmax records of a step live in a ring of two tiles: in a walk of
+//    consecutive tiles the consumers past this tile's end are the first rows
+//    of the previous step's tile, so only the first step computes them.
+
+#include <type_traits>
 
 #include "sbda_common.cuh"
 
@@ -190,7 +204,9 @@ __device__ __forceinline__ void tma_qd_slot(const BwdMaps& maps, const BwdV2Para
 // Source-set shapes the backward is compiled for.  0 reads the flags at run
 // time; the others fix them so the per-row code is straight-line:
 //   1: {0, 1} (SBDA layer 1)          2: {0, 2} (SBDA layer 2)
-//   3: {0, 1, 2, d}, d < TILE (local) 4: {0, 1, 2, d}, d % TILE == 0 (chain walk)
+//   3: {0, 1, 2, d}, d < TILE, d % 4 == 0 (local carry)
+//   4: {0, 1, 2, d}, d % TILE == 0 (chain walk)
+//   5: {0, 1, 2, d}, d < TILE (local)
 template <int SHAPE>
 struct BwdShape {
   static constexpr bool kGeneric = SHAPE == 0;
@@ -198,6 +214,7 @@ struct BwdShape {
   static constexpr bool kHas2 = SHAPE >= 2;
   static constexpr bool kFar = SHAPE >= 3;
   static constexpr bool kChain = SHAPE == 4;
+  static constexpr bool kLocalCarry = SHAPE == 3;
 };
 
 template <typename TE, int LPR, bool TMA, int SHAPE>
@@ -217,11 +234,13 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
   const bool has2 = Sh::kGeneric ? g.has2 != 0 : Sh::kHas2;
   const bool far = Sh::kGeneric ? g.has_far != 0 : Sh::kFar;
   const bool chain = Sh::kGeneric ? g.mode == 0 : Sh::kChain;
-  const int Hc = (Sh::kChain || SHAPE == 1 || SHAPE == 2) ? 2 : g.halo;  // consumer rows past the tile
-  const int KVR = T + 2 * Hc;  // rows of a K/V slot
-  const int QDR = T + Hc;      // rows of a Q/dO slot
-  const int nkv = chain ? 2 : 1;
+  const bool lc = Sh::kGeneric ? g.mode == 2 : Sh::kLocalCarry;
+  const int Hc = (Sh::kGeneric || SHAPE == 5) ? g.halo : 2;  // consumer rows past the tile
   const int d = g.d;
+  const int lead = lc ? d : Hc;                  // K/V rows of a near slot before the tile
+  const int KVR = lc ? T + d : T + 2 * Hc;       // rows of a K/V slot
+  const int QDR = T + Hc;                        // rows of a Q/dO slot
+  const int nkv = chain ? 2 : 1;
 
   // ---- Work assignment: a walk of tiles for this CTA. ----
   // Heads vary fastest across consecutive CTAs: the rows of all heads of a
@@ -250,18 +269,22 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     const int lo = s * g.seg;
     if (lo >= g.nT) return;
     const int hi = min(lo + g.seg, g.nT) - 1;
-    pre = 0;
-    t_first = hi;
-    n_steps = hi - lo + 1;
+    pre = lc && hi + 1 < g.nT;
+    t_first = hi + pre;
+    n_steps = hi - lo + 1 + pre;
     stride = 1;
   }
 
   uint8_t* KVbase = smem;                        // nkv slots of [K rows][V rows]
   uint8_t* QDbase = KVbase + nkv * 2 * KVR * P;  // 2 slots of [Q rows][dO rows]
-  // Per consumer: (p0, ds0, p1, ds1) (p2, ds2, pf, dsf); ds already scaled by head_dim^-0.5.
-  float4* E = reinterpret_cast<float4*>(QDbase + 2 * 2 * QDR * P);
+  // Softmax records, a ring of 2T consumers: (p0, ds0, p1, ds1) (p2, ds2, pf, dsf)
+  // per consumer, ds already scaled by head_dim^-0.5.  Consumer c of step s sits
+  // at ring row (s * T + c) mod 2T, so rows T.. of a step are rows 0.. of the
+  // step before.  Every 4 rows carry 16 bytes of padding: the row groups of a
+  // warp (4 rows apart) then start on different banks.
+  float* E = reinterpret_cast<float*>(QDbase + 2 * 2 * QDR * P);
   // Two LSE slots of lse_box fp32 rows each (128-byte multiples), 128-byte aligned after E.
-  float* LSEs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(E + QDR * 2) + 127) & ~uintptr_t(127));
+  float* LSEs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(E + v2_ring_floats(T)) + 127) & ~uintptr_t(127));
   uint64_t* bars = reinterpret_cast<uint64_t*>(LSEs + 2 * p.lse_box);
   auto kslot = [&](int s) { return KVbase + s * 2 * KVR * P; };
   auto vslot = [&](int s) { return KVbase + s * 2 * KVR * P + KVR * P; };
@@ -292,16 +315,23 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     if constexpr (TMA) {
       uint64_t* bar = bars + (i & 1);
       mbar_arrive_expect_tx(bar, (uint32_t)((chain && i == 0 ? 2 : 1) * 2 * KVR * P));
-      for (int part = first; part < (chain ? 2 : 1); ++part) {
-        const int slot = chain ? ((i + part) & 1) : 0;
-        const int p0 = part == 0 ? j0 - Hc : j0 - d - Hc;
-        tma_kv_slot<TE, T, P>(maps, p, bar, kslot(slot), vslot(slot), p0, Hc, h, b);
+      if (lc) {  // rows [j0 - d, j0 + T): a d-row box, then the tile
+        tma_rows(kslot(0), &maps.kH, bar, p.slots_k, j0 - d, h, b);
+        tma_rows(vslot(0), &maps.vH, bar, p.slots_v, j0 - d, h, b);
+        tma_rows(kslot(0) + d * P, &maps.kT, bar, p.slots_k, j0, h, b);
+        tma_rows(vslot(0) + d * P, &maps.vT, bar, p.slots_v, j0, h, b);
+      } else {
+        for (int part = first; part < (chain ? 2 : 1); ++part) {
+          const int slot = chain ? ((i + part) & 1) : 0;
+          const int p0 = part == 0 ? j0 - Hc : j0 - d - Hc;
+          tma_kv_slot<TE, T, P>(maps, p, bar, kslot(slot), vslot(slot), p0, Hc, h, b);
+        }
       }
     } else {
       constexpr int PE = P / sizeof(TE);
       for (int part = first; part < (chain ? 2 : 1); ++part) {
         const int slot = chain ? ((i + part) & 1) : 0;
-        const int p0 = part == 0 ? j0 - Hc : j0 - d - Hc;
+        const int p0 = part == 0 ? j0 - lead : j0 - d - Hc;
         generic_rows<TE>(kslot(slot), p.k, b, h, p0, KVR, p.L, p.D, PE);
         generic_rows<TE>(vslot(slot), p.v, b, h, p0, KVR, p.L, p.D, PE);
       }
@@ -334,17 +364,19 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
 #pragma unroll
   for (int i = 0; i < 4; ++i) carry_k[i] = carry_v[i] = frag_zero();
 
-#pragma unroll 1
-  for (int step = 0; step < n_steps; ++step) {
+  // One step of the walk.  The carry-only "pre" tile is a separate instance
+  // (PreTag = true_type), so the steady-state loop has no per-step pre tests.
+  // Returns false when a copy wait expired; the CTA then stops.
+  auto run_step = [&](const int step, auto pre_tag) -> bool {
+    constexpr bool is_pre = decltype(pre_tag)::value;
     const int t = t_first - step * stride;
     const int j0 = t * T;
-    const bool is_pre = pre && step == 0;
     if constexpr (TMA) {
       if (tid == 0 && step + 1 < n_steps) issue_qd(step + 1);
       const bool ok = mbar_wait_bounded(bars + (step & 1), (step >> 1) & 1);
       if (__syncthreads_or(!ok)) {
         fault_and_drain(p.status, bars + (step & 1), (step >> 1) & 1);
-        return;
+        return false;
       }
     } else {
       issue_qd(step);
@@ -356,13 +388,21 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     const uint8_t* VN = vslot(ns);
     const uint8_t* KF = chain ? kslot(ns ^ 1) : KN;
     const uint8_t* VF = chain ? vslot(ns ^ 1) : VN;
-    const int fidx = chain ? Hc : Hc - d;  // far source row of consumer c = c + fidx
+    const int fidx = chain ? Hc : lead - d;  // far source row of consumer c = c + fidx
     const uint8_t* Qs = qslot(step & 1);
     const uint8_t* Ds = dslot(step & 1);
+    const int ebase = (step & 1) * T;
+    // Record of consumer c: ring row x = (ebase + c) mod 2T at float x * 8 + (x / 4) * 4,
+    // i.e. 9 * x for x a multiple of 4 and 8 floats further per row after it.
+    auto erec = [&](int c) -> float* {
+      const int x = (ebase + c) & (2 * T - 1);
+      return E + x * 8 + (x >> 2) * 4;
+    };
+    auto egroup = [&](int c4) -> float* { return E + 9 * ((ebase + c4) & (2 * T - 1)); };  // c4 % 4 == 0
 
     // ---- Phase 1: softmax terms of every consumer, dQ of own queries. ----
-    auto consume = [&](int c, bool act, const Frag& k0, const Frag& v0, const Frag& k1, const Frag& v1,
-                       const Frag& k2, const Frag& v2, float lq2) {
+    auto consume = [&](int c, bool act, float* erow, const Frag& k0, const Frag& v0, const Frag& k1,
+                       const Frag& v1, const Frag& k2, const Frag& v2, float lq2) {
       const int q = j0 + c;
       const Frag qf = FragIO<TE>::load(Qs + c * P, l);
       const Frag df = FragIO<TE>::load(Ds + c * P, l);
@@ -402,26 +442,28 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
         store_frag<TE, TMA>(dq + (long long)q * p.dq.sl, p.dq.sd, p.D, l, gq);
       }
       if (act && l == 0) {
-        E[c * 2] = make_float4(p0, d0, p1, d1);
-        E[c * 2 + 1] = make_float4(p2, d2, pf, dfw);
+        float4* e = reinterpret_cast<float4*>(erow);
+        e[0] = make_float4(p0, d0, p1, d1);
+        e[1] = make_float4(p2, d2, pf, dfw);
       }
     };
 
     {
       const int a = grp * 4;
       float lq[4];
-#pragma unroll
       const float* ls = LSEs + (step & 1) * p.lse_box;
+#pragma unroll
       for (int i = 0; i < 4; ++i)
         lq[i] = (TMA && p.lse_tma) ? ls[a + i] * kLog2e : ((j0 + a + i < p.L) ? lse[j0 + a + i] * kLog2e : 0.f);
-      Frag k1 = FragIO<TE>::load(KN + (a + Hc - 1) * P, l), k2 = FragIO<TE>::load(KN + (a + Hc - 2) * P, l);
-      Frag v1 = FragIO<TE>::load(VN + (a + Hc - 1) * P, l), v2 = FragIO<TE>::load(VN + (a + Hc - 2) * P, l);
+      Frag k1 = FragIO<TE>::load(KN + (a + lead - 1) * P, l), k2 = FragIO<TE>::load(KN + (a + lead - 2) * P, l);
+      Frag v1 = FragIO<TE>::load(VN + (a + lead - 1) * P, l), v2 = FragIO<TE>::load(VN + (a + lead - 2) * P, l);
+      float* Eg = egroup(a);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int c = a + i;
-        const Frag k0 = FragIO<TE>::load(KN + (c + Hc) * P, l);
-        const Frag v0 = FragIO<TE>::load(VN + (c + Hc) * P, l);
-        consume(c, true, k0, v0, k1, v1, k2, v2, lq[i]);
+        const Frag k0 = FragIO<TE>::load(KN + (c + lead) * P, l);
+        const Frag v0 = FragIO<TE>::load(VN + (c + lead) * P, l);
+        consume(c, true, Eg + 8 * i, k0, v0, k1, v1, k2, v2, lq[i]);
         k2 = k1;
         k1 = k0;
         v2 = v1;
@@ -429,25 +471,30 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
       }
     }
     // Consumers past the tile: runs of xr rows; warps with no live row skip.
-    {
+    // A walk of consecutive tiles has them from the step before; in local carry
+    // mode only their near sources are read, and the first step of a walk
+    // without a pre tile starts at the sequence end, where they are empty.
+    if (lc) {
+      if (step == 0 && !pre && tid < 2 * 8) erec(T + (tid >> 3))[tid & 7] = 0.f;
+    } else if (stride != 1 || step == 0) {
       const int xr = (Hc + GROUPS - 1) / GROUPS;
       const int warp_first = (tid >> 5) * GPW * xr;
       if (warp_first < Hc) {
         const int e0 = grp * xr;
         const int cbase = T + min(e0, Hc - 1);
-        Frag k1 = FragIO<TE>::load(KN + (cbase + Hc - 1) * P, l);
-        Frag k2 = FragIO<TE>::load(KN + (cbase + Hc - 2) * P, l);
-        Frag v1 = FragIO<TE>::load(VN + (cbase + Hc - 1) * P, l);
-        Frag v2 = FragIO<TE>::load(VN + (cbase + Hc - 2) * P, l);
+        Frag k1 = FragIO<TE>::load(KN + (cbase + lead - 1) * P, l);
+        Frag k2 = FragIO<TE>::load(KN + (cbase + lead - 2) * P, l);
+        Frag v1 = FragIO<TE>::load(VN + (cbase + lead - 1) * P, l);
+        Frag v2 = FragIO<TE>::load(VN + (cbase + lead - 2) * P, l);
 #pragma unroll 1
         for (int i = 0; i < xr; ++i) {
           const bool act = e0 + i < Hc;
           const int c = act ? T + e0 + i : cbase;
           const float lq = (TMA && p.lse_tma) ? LSEs[(step & 1) * p.lse_box + c] * kLog2e
                                               : ((act && j0 + c < p.L) ? lse[j0 + c] * kLog2e : 0.f);
-          const Frag k0 = FragIO<TE>::load(KN + (c + Hc) * P, l);
-          const Frag v0 = FragIO<TE>::load(VN + (c + Hc) * P, l);
-          consume(c, act, k0, v0, k1, v1, k2, v2, lq);
+          const Frag k0 = FragIO<TE>::load(KN + (c + lead) * P, l);
+          const Frag v0 = FragIO<TE>::load(VN + (c + lead) * P, l);
+          consume(c, act, erec(c), k0, v0, k1, v1, k2, v2, lq);
           k2 = k1;
           k1 = k0;
           v2 = v1;
@@ -465,35 +512,54 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
 
     // ---- Phase 2: dK / dV of own keys, gathered from their consumers. ----
     {
-      const float2* E2 = reinterpret_cast<const float2*>(E);  // [c][4] (p, ds) per source
       const int a = grp * 4;
-      Frag q1 = FragIO<TE>::load(Qs + (a + 1) * P, l), d1 = FragIO<TE>::load(Ds + (a + 1) * P, l);
-      Frag q0 = FragIO<TE>::load(Qs + a * P, l), d0 = FragIO<TE>::load(Ds + a * P, l);
+      // Local carry: keys a - d .. a - d + 3 (mod T); "carried" groups hold the
+      // last d keys, whose far consumers a .. a + 3 lie in the previous step's tile.
+      const bool carried = lc && a < d;
+      const int r0 = lc ? (carried ? a - d + T : a - d) : a;
+      // Records r0 + j (j = 0..5, fixed after unrolling) and the group's own rows a + i.
+      const float* Ea = egroup(r0);
+      const float* Eb = egroup(r0 + 4);
+      const float* Eo = egroup(a);
+      auto rec = [&](int j, int src) {
+        return *reinterpret_cast<const float2*>((j < 4 ? Ea + 8 * j : Eb + 8 * (j - 4)) + 2 * src);
+      };
+      Frag q1 = FragIO<TE>::load(Qs + (r0 + 1) * P, l), d1 = FragIO<TE>::load(Ds + (r0 + 1) * P, l);
+      Frag q0 = FragIO<TE>::load(Qs + r0 * P, l), d0 = FragIO<TE>::load(Ds + r0 * P, l);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int r = a + i;
+        const int r = r0 + i;
         const Frag q2 = FragIO<TE>::load(Qs + (r + 2) * P, l);
         const Frag d2 = FragIO<TE>::load(Ds + (r + 2) * P, l);
+        Frag qf, df;  // local carry: the group's own consumer row a + i
+        if (lc) {
+          qf = FragIO<TE>::load(Qs + (a + i) * P, l);
+          df = FragIO<TE>::load(Ds + (a + i) * P, l);
+        }
         if (!is_pre) {
           Frag ak = carry_k[i], av = carry_v[i];
           if (has0) {
-            const float2 e = E2[r * 4 + 0];
+            const float2 e = rec(i, 0);
             frag_axpy(ak, e.y, q0);
             frag_axpy(av, e.x, d0);
           }
           if (has1) {
-            const float2 e = E2[(r + 1) * 4 + 1];
+            const float2 e = rec(i + 1, 1);
             frag_axpy(ak, e.y, q1);
             frag_axpy(av, e.x, d1);
           }
           if (has2) {
-            const float2 e = E2[(r + 2) * 4 + 2];
+            const float2 e = rec(i + 2, 2);
             frag_axpy(ak, e.y, q2);
             frag_axpy(av, e.x, d2);
           }
-          if (far && !chain) {
+          if (lc && !carried) {
+            const float2 e = *reinterpret_cast<const float2*>(Eo + 8 * i + 6);
+            frag_axpy(ak, e.y, qf);
+            frag_axpy(av, e.x, df);
+          } else if (far && !chain && !lc) {
             const int c = r + d;
-            const float2 e = E2[c * 4 + 3];
+            const float2 e = *reinterpret_cast<const float2*>(erec(c) + 6);
             frag_axpy(ak, e.y, FragIO<TE>::load(Qs + c * P, l));
             frag_axpy(av, e.x, FragIO<TE>::load(Ds + c * P, l));
           }
@@ -504,9 +570,14 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
           }
         }
         if (chain && far) {
-          const float2 e = E2[r * 4 + 3];
+          const float2 e = rec(i, 3);
           carry_k[i] = frag_mul(e.y, q0);
           carry_v[i] = frag_mul(e.x, d0);
+        }
+        if (carried) {
+          const float2 e = *reinterpret_cast<const float2*>(Eo + 8 * i + 6);
+          carry_k[i] = frag_mul(e.y, qf);
+          carry_v[i] = frag_mul(e.x, df);
         }
         q0 = q1;
         d0 = d1;
@@ -515,7 +586,17 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
       }
     }
     __syncthreads();  // slots of this step are refilled by later copies
+    return true;
+  };
+
+  int first = 0;
+  if (pre) {
+    if (!run_step(0, std::true_type{})) return;
+    first = 1;
   }
+#pragma unroll 1
+  for (int step = first; step < n_steps; ++step)
+    if (!run_step(step, std::false_type{})) return;
 }
 
 // --------------------------------------------------------------------------
@@ -563,7 +644,7 @@ int fwd_v2_lpr(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cuda
 int bwd_shape(const V2Geometry& g) {
   if (g.has0 && g.has1 && !g.has2 && !g.has_far) return 1;
   if (g.has0 && !g.has1 && g.has2 && !g.has_far) return 2;
-  if (g.has0 && g.has1 && g.has2 && g.has_far) return g.mode == 0 ? 4 : 3;
+  if (g.has0 && g.has1 && g.has2 && g.has_far) return g.mode == 0 ? 4 : (g.mode == 2 ? 3 : 5);
   return 0;
 }
 
@@ -577,6 +658,7 @@ int bwd_v2_lpr(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cuda
         case 2: return launch_bwd_v2<TE, 8, TMA, 2>(maps, p, pl, st);
         case 3: return launch_bwd_v2<TE, 8, TMA, 3>(maps, p, pl, st);
         case 4: return launch_bwd_v2<TE, 8, TMA, 4>(maps, p, pl, st);
+        case 5: return launch_bwd_v2<TE, 8, TMA, 5>(maps, p, pl, st);
         default: break;
       }
     }

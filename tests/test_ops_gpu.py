@@ -255,3 +255,44 @@ def test_module_matches_reference_golden(golden):
         for pname, param in module.named_parameters():
             torch.testing.assert_close(param.grad.cpu(), golden.get(name, "grad." + pname), **tol,
                                        msg=f"{name} {pname}")
+
+
+def test_config2_full_parity():
+    """Config 2: B 4, 8 heads x 64, L 32768, layer 10 (offsets 0, 1, 2, 512), bf16, vs the fp32 oracle."""
+    q, k, v, do = _inputs(4, 8, 32768, 64, torch.bfloat16, seed=2)
+    offsets = sbda_b200.topology_offsets(10)
+    out, dq, dk, dv = _run(q, k, v, do, offsets)
+    ro, rdq, rdk, rdv = orc.exact_attention_grads(q, k, v, offsets, do)
+    for name, got, ref in (("O", out, ro), ("dQ", dq, rdq), ("dK", dk, rdk), ("dV", dv, rdv)):
+        _close(got, ref, torch.bfloat16, f"config 2 {name}")
+
+
+def test_config3_stack_sampled_rows():
+    """Config 3: B 8, 8 heads x 64, L 32768, all 15 SBDA layers, bf16.
+
+    The kernels run on the whole batch; sampled rows of the first and last batch entries are
+    checked against the fp64 row oracle (the rest of the batch shares the same code path).
+    """
+    g = torch.Generator().manual_seed(3)
+    rows = torch.cat([torch.tensor([0, 1, 2, 3, 63, 64, 65, 16383, 16384, 32767]),
+                      torch.randint(0, 32768, (60,), generator=g)])
+    batches = torch.tensor([0, 7])
+    dev_rows, dev_batches = rows.cuda(), batches.cuda()
+    for layer in range(1, 16):
+        offsets = sbda_b200.topology_offsets(layer, total_layers=15)
+        q, k, v, do = _inputs(8, 8, 32768, 64, torch.bfloat16, seed=300 + layer)
+        out, dq, dk, dv = _run(q, k, v, do, offsets)
+        qc, kc, vc, doc = (t.detach()[dev_batches].cpu() for t in (q, k, v, do))
+        ro, rdq = orc.query_rows(qc, kc, vc, doc, offsets, rows)
+        rdk, rdv = orc.key_rows(qc, kc, vc, doc, offsets, rows)
+        for name, got, ref in (("O", out, ro), ("dQ", dq, rdq), ("dK", dk, rdk), ("dV", dv, rdv)):
+            _close(got[dev_batches][:, :, dev_rows], ref, torch.bfloat16, f"config 3 layer {layer} {name}")
+
+
+@pytest.mark.parametrize("length", [64, 65, 4099, 20000])
+def test_local_carry_offsets(length, kernel_path):
+    """Far offsets below the tile height: the local walk (small d, or d not a multiple of 4)
+    and the carried local walk (d % 4 == 0 with d large enough that local staging would
+    lower occupancy), with and without near offsets, across segment boundaries and ragged ends."""
+    for offsets in ((0, 1, 2, 4), (0, 1, 2, 12), (0, 1, 2, 32), (0, 1, 2, 60), (0, 2, 48), (0, 8), (0, 1, 2, 6)):
+        _check(1, 4, length, 64, torch.bfloat16, offsets, seed=length + offsets[-1])
