@@ -382,7 +382,10 @@ template <>
 struct FragIO<__nv_bfloat16> {
   static constexpr int kLaneBytes = 16;
   static __device__ __forceinline__ Frag load(const uint8_t* row, int l) {
-    const uint4 u = *reinterpret_cast<const uint4*>(row + l * 16);
+    return from_words(reinterpret_cast<const uint4*>(row + l * 16));
+  }
+  static __device__ __forceinline__ Frag from_words(const uint4* w) {
+    const uint4 u = w[0];
     Frag f;
     f.v[0] = make_float2(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u));
     f.v[1] = make_float2(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
@@ -400,7 +403,10 @@ template <>
 struct FragIO<__half> {
   static constexpr int kLaneBytes = 16;
   static __device__ __forceinline__ Frag load(const uint8_t* row, int l) {
-    const uint4 u = *reinterpret_cast<const uint4*>(row + l * 16);
+    return from_words(reinterpret_cast<const uint4*>(row + l * 16));
+  }
+  static __device__ __forceinline__ Frag from_words(const uint4* w) {
+    const uint4 u = w[0];
     Frag f;
     f.v[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
     f.v[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
@@ -419,8 +425,11 @@ template <>
 struct FragIO<float> {
   static constexpr int kLaneBytes = 32;
   static __device__ __forceinline__ Frag load(const uint8_t* row, int l) {
-    const float4 a = *reinterpret_cast<const float4*>(row + l * 32);
-    const float4 b = *reinterpret_cast<const float4*>(row + l * 32 + 16);
+    return from_words(reinterpret_cast<const uint4*>(row + l * 32));
+  }
+  static __device__ __forceinline__ Frag from_words(const uint4* w) {
+    const float4 a = *reinterpret_cast<const float4*>(&w[0]);
+    const float4 b = *reinterpret_cast<const float4*>(&w[1]);
     Frag f;
     f.v[0] = make_float2(a.x, a.y);
     f.v[1] = make_float2(a.z, a.w);
@@ -429,6 +438,28 @@ struct FragIO<float> {
     return f;
   }
 };
+
+// One lane's part of a row read straight from global memory, still packed
+// (16-byte words).  Vector layouts only: 16-byte aligned rows, unit channel
+// stride, D * element size a multiple of 16.  Channels past D, and every
+// channel when `live` is false, read as zero.
+template <typename TE>
+struct RowWords {
+  uint4 w[FragIO<TE>::kLaneBytes / 16];
+};
+
+template <typename TE>
+__device__ __forceinline__ RowWords<TE> load_row_words(const TE* row, int D, int l, bool live) {
+  constexpr int kEpw = 16 / sizeof(TE);  // elements per 16-byte word
+  RowWords<TE> r;
+#pragma unroll
+  for (int i = 0; i < FragIO<TE>::kLaneBytes / 16; ++i) {
+    const int c = l * 8 + i * kEpw;
+    r.w[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (live && c < D) r.w[i] = __ldg(reinterpret_cast<const uint4*>(row + c));
+  }
+  return r;
+}
 
 __device__ __forceinline__ float frag_dot(const Frag& a, const Frag& b) {
   float2 acc = make_float2(0.f, 0.f);
@@ -492,6 +523,44 @@ __device__ __forceinline__ float lane_group_sum(float x) {
 #pragma unroll
   for (int m = LPR / 2; m >= 1; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m);
   return x;
+}
+
+// Reduce-scatter over the 8 lanes of a row group (lane index l = lane % 8):
+// eight per-lane partial sums in, the group total of x[l] out on lane l.
+// Three halving exchanges (4 + 2 + 1 shuffles) instead of eight all-reduces.
+__device__ __forceinline__ float group8_reduce_scatter8(const float (&x)[8], int l) {
+  const unsigned full = 0xffffffffu;
+  const bool h4 = l & 4, h2 = l & 2, h1 = l & 1;
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h4 ? x[i] : x[i + 4];
+    w[i] = (h4 ? x[i + 4] : x[i]) + __shfl_xor_sync(full, send, 4);
+  }
+  float z[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h2 ? w[i] : w[i + 2];
+    z[i] = (h2 ? w[i + 2] : w[i]) + __shfl_xor_sync(full, send, 2);
+  }
+  const float send = h1 ? z[0] : z[1];
+  return (h1 ? z[1] : z[0]) + __shfl_xor_sync(full, send, 1);
+}
+
+// Four per-lane partial sums over the 8 lanes of a row group: the group total
+// of x[k] out on lanes 2k and 2k + 1.
+__device__ __forceinline__ float group8_reduce_scatter4(const float (&x)[4], int l) {
+  const unsigned full = 0xffffffffu;
+  const bool h4 = l & 4, h2 = l & 2;
+  float w[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h4 ? x[i] : x[i + 2];
+    w[i] = (h4 ? x[i + 2] : x[i]) + __shfl_xor_sync(full, send, 4);
+  }
+  const float send = h2 ? w[0] : w[1];
+  const float z = (h2 ? w[1] : w[0]) + __shfl_xor_sync(full, send, 2);
+  return z + __shfl_xor_sync(full, z, 1);
 }
 
 // --------------------------------------------------------------------------

@@ -84,13 +84,17 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   const bool far = SHAPE == 0 ? g.has_far != 0 : SHAPE == 3;
   const bool has0 = SHAPE == 0 ? g.has0 != 0 : true;
 
+  // The copy-engine path reads each group's Q rows straight into registers
+  // (no Q tile in shared memory: more CTAs per SM); the generic path stages Q.
   uint8_t* Qs = smem;
-  uint8_t* Kn = Qs + T * P;  // positions [i0-2, i0+T)
+  uint8_t* Kn = smem + (TMA ? 0 : T * P);  // positions [i0-2, i0+T)
   uint8_t* Vn = Kn + (T + 2) * P;
   uint8_t* Kf = Vn + (T + 2) * P;  // positions [i0-d, i0-d+T)
   uint8_t* Vf = Kf + (far ? T * P : 0);
   uint64_t* bar = reinterpret_cast<uint64_t*>(Vf + (far ? T * P : 0));
 
+  const int a = grp * 4;
+  RowWords<TE> qw[4];
   if constexpr (TMA) {
     if (tid == 0) {
       mbar_init(bar, 1);
@@ -98,8 +102,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
     }
     __syncthreads();
     if (tid == 0) {
-      mbar_arrive_expect_tx(bar, (uint32_t)((T * (3 + 2 * far) + 4) * P));
-      tma_rows(Qs, &maps.qT, bar, p.slots_q, i0, h, b);
+      mbar_arrive_expect_tx(bar, (uint32_t)((T * (2 + 2 * far) + 4) * P));
       tma_rows(Kn, &maps.kH, bar, p.slots_k, i0 - 2, h, b);
       tma_rows(Vn, &maps.vH, bar, p.slots_v, i0 - 2, h, b);
       tma_rows(Kn + 2 * P, &maps.kT, bar, p.slots_k, i0, h, b);
@@ -108,6 +111,13 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
         tma_rows(Kf, &maps.kT, bar, p.slots_k, i0 - g.d, h, b);
         tma_rows(Vf, &maps.vT, bar, p.slots_v, i0 - g.d, h, b);
       }
+    }
+    // Q rows of this group, in flight while the K/V copies land.
+    const TE* qb = reinterpret_cast<const TE*>(p.q.ptr) + (long long)b * p.q.sb + (long long)h * p.q.sh;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pos = i0 + a + i;
+      qw[i] = load_row_words<TE>(qb + (long long)min(pos, p.L - 1) * p.q.sl, p.D, l, pos < p.L);
     }
     const bool ok = mbar_wait_bounded(bar, 0);
     if (__syncthreads_or(!ok)) {
@@ -130,15 +140,60 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   TE* out = reinterpret_cast<TE*>(const_cast<void*>(p.out.ptr)) + (long long)b * p.out.sb +
             (long long)h * p.out.sh;
   float* lse = p.lse + ((long long)b * p.H + h) * p.L;
-  const int a = grp * 4;
+  // Source owned by this lane pair in the reduce-scatter softmax (8 lanes per row).
+  const int src_k = (l >> 1) & 3;
+  const bool src_has = src_k == 0 ? has0 : (src_k == 1 ? has1 : (src_k == 2 ? has2 : far));
+  const int src_off = src_k == 0 ? 0 : (src_k == 1 ? 1 : (src_k == 2 ? 2 : g.d));
   Frag k1 = FragIO<TE>::load(Kn + (a + 1) * P, l), k2 = FragIO<TE>::load(Kn + a * P, l);
   Frag v1 = FragIO<TE>::load(Vn + (a + 1) * P, l), v2 = FragIO<TE>::load(Vn + a * P, l);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = a + i, pos = i0 + r;
-    const Frag q = FragIO<TE>::load(Qs + r * P, l);
+    const Frag q = TMA ? FragIO<TE>::from_words(qw[i].w) : FragIO<TE>::load(Qs + r * P, l);
     const Frag k0 = FragIO<TE>::load(Kn + (r + 2) * P, l);
     const Frag v0 = FragIO<TE>::load(Vn + (r + 2) * P, l);
+    if constexpr (LPR == 8) {
+      // Reduce-scatter softmax: lanes 2k and 2k + 1 of the group hold the score of
+      // source k; max, exponent and sum are formed once per source.
+      float x[4];
+      x[0] = frag_dot(q, k0);
+      x[1] = has1 ? frag_dot(q, k1) : 0.f;
+      x[2] = has2 ? frag_dot(q, k2) : 0.f;
+      x[3] = 0.f;
+      Frag vf;
+      if (far) {
+        const Frag kf = FragIO<TE>::load(Kf + r * P, l);
+        x[3] = frag_dot(q, kf);
+        vf = FragIO<TE>::load(Vf + r * P, l);
+      }
+      const unsigned full = 0xffffffffu;
+      const float val = group8_reduce_scatter4(x, l);
+      const bool live = src_has && pos >= src_off;
+      const float sc = live ? val * c1 : -INFINITY;  // log2 units
+      float m = fmaxf(sc, __shfl_xor_sync(full, sc, 2));
+      m = fmaxf(m, __shfl_xor_sync(full, m, 4));
+      const bool any = m != -INFINITY;
+      const float e = live ? fast_exp2(sc - m) : 0.f;
+      float sum = e + __shfl_xor_sync(full, e, 2);
+      sum += __shfl_xor_sync(full, sum, 4);
+      const float inv = any ? __frcp_rn(sum) : 0.f;
+      const float w = e * inv;
+      const float w0 = __shfl_sync(full, w, 0, 8), w1 = __shfl_sync(full, w, 2, 8);
+      const float w2 = __shfl_sync(full, w, 4, 8), wf = __shfl_sync(full, w, 6, 8);
+      Frag o = frag_mul(w0, v0);
+      if (has1) frag_axpy(o, w1, v1);
+      if (has2) frag_axpy(o, w2, v2);
+      if (far) frag_axpy(o, wf, vf);
+      if (pos < p.L) {
+        store_frag<TE, TMA>(out + (long long)pos * p.out.sl, p.out.sd, p.D, l, o);
+        if (l == 0) lse[pos] = any ? (m + __log2f(sum)) * kLn2 : -INFINITY;
+      }
+      k2 = k1;
+      k1 = k0;
+      v2 = v1;
+      v1 = v0;
+      continue;
+    }
     float s0 = lane_group_sum<LPR>(frag_dot(q, k0));
     float s1 = has1 ? lane_group_sum<LPR>(frag_dot(q, k1)) : 0.f;
     float s2 = has2 ? lane_group_sum<LPR>(frag_dot(q, k2)) : 0.f;
@@ -237,6 +292,10 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
   const bool lc = Sh::kGeneric ? g.mode == 2 : Sh::kLocalCarry;
   const int Hc = (Sh::kGeneric || SHAPE == 5) ? g.halo : 2;  // consumer rows past the tile
   const int d = g.d;
+  // Source owned by this lane in the reduce-scatter softmax (8 lanes per row).
+  const int src_k = l & 3;
+  const bool src_has = src_k == 0 ? has0 : (src_k == 1 ? has1 : (src_k == 2 ? has2 : far));
+  const int src_off = src_k == 0 ? 0 : (src_k == 1 ? 1 : (src_k == 2 ? 2 : d));
   const int lead = lc ? d : Hc;                  // K/V rows of a near slot before the tile
   const int KVR = lc ? T + d : T + 2 * Hc;       // rows of a K/V slot
   const int QDR = T + Hc;                        // rows of a Q/dO slot
@@ -406,6 +465,46 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
       const int q = j0 + c;
       const Frag qf = FragIO<TE>::load(Qs + c * P, l);
       const Frag df = FragIO<TE>::load(Ds + c * P, l);
+      if constexpr (LPR == 8) {
+        // Reduce-scatter softmax: after the exchange lane l holds q.k of source l
+        // (l < 4) or dO.v of source l - 4; each source's p and ds are formed once.
+        float x[8];
+        x[0] = frag_dot(qf, k0);
+        x[4] = frag_dot(df, v0);
+        x[1] = has1 ? frag_dot(qf, k1) : 0.f;
+        x[5] = has1 ? frag_dot(df, v1) : 0.f;
+        x[2] = has2 ? frag_dot(qf, k2) : 0.f;
+        x[6] = has2 ? frag_dot(df, v2) : 0.f;
+        x[3] = x[7] = 0.f;
+        Frag kf;
+        if (far) {
+          kf = FragIO<TE>::load(KF + (c + fidx) * P, l);
+          const Frag vf = FragIO<TE>::load(VF + (c + fidx) * P, l);
+          x[3] = frag_dot(qf, kf);
+          x[7] = frag_dot(df, vf);
+        }
+        const unsigned full = 0xffffffffu;
+        const float val = group8_reduce_scatter8(x, l);
+        const bool inr = q < p.L;
+        const bool live = l < 4 && src_has && inr && q >= src_off;
+        const float pa = live ? fast_exp2(fmaf(val, c1, -lq2)) : 0.f;
+        const float ps = __shfl_xor_sync(full, pa, 4);  // lanes 4..7: p of source l - 4
+        const float t = l >= 4 ? ps * val : 0.f;
+        float delta = t + __shfl_xor_sync(full, t, 1);
+        delta += __shfl_xor_sync(full, delta, 2);
+        const float ds = ps * (val - delta) * scale;  // lanes 4..7
+        const float d0 = __shfl_sync(full, ds, 4, 8), d1 = __shfl_sync(full, ds, 5, 8);
+        const float d2 = __shfl_sync(full, ds, 6, 8), dfw = __shfl_sync(full, ds, 7, 8);
+        if (act && c < T && inr && !is_pre) {
+          Frag gq = frag_mul(d0, k0);
+          if (has1) frag_axpy(gq, d1, k1);
+          if (has2) frag_axpy(gq, d2, k2);
+          if (far) frag_axpy(gq, dfw, kf);
+          store_frag<TE, TMA>(dq + (long long)q * p.dq.sl, p.dq.sd, p.D, l, gq);
+        }
+        if (act && l >= 4) reinterpret_cast<float2*>(erow)[l - 4] = make_float2(ps, ds);
+        return;
+      }
       const float a0 = lane_group_sum<LPR>(frag_dot(qf, k0));
       const float b0 = lane_group_sum<LPR>(frag_dot(df, v0));
       float a1 = 0.f, b1 = 0.f, a2 = 0.f, b2 = 0.f, af = 0.f, bf = 0.f;
@@ -606,10 +705,12 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
 template <typename TE, int LPR, bool TMA, int SHAPE>
 int launch_fwd_v2(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
   auto kern = sbda_fwd_v2_kernel<TE, LPR, TMA, SHAPE>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_fwd) != cudaSuccess)
+  // The copy-engine path keeps Q out of shared memory.
+  const size_t smem = pl.smem_fwd - (TMA ? (size_t)v2_tile(LPR) * pl.pitch : 0);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SBDA_ERR_CUDA;
   const long long blocks = (long long)p.B * p.H * pl.g.nT;
-  kern<<<(unsigned)blocks, kThreads, pl.smem_fwd, st>>>(maps, p);
+  kern<<<(unsigned)blocks, kThreads, smem, st>>>(maps, p);
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
