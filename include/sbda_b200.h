@@ -186,8 +186,10 @@ int sbda_b200_norm_rope_backward_noalloc(int dtype, sbda_shape shape, sbda_tenso
 /*
  * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
  * (the windowed chain-walking kernels wherever they apply, else the general
- * ones), 1 = general kernels only.  Returns the previous setting, or -1 for
- * an unknown value.  Both families compute the same function.
+ * ones, else the uniform ones), 1 = general kernels (uniform ones for offset
+ * sets with several far offsets), 2 = uniform kernels only.  Returns the
+ * previous setting, or -1 for an unknown value.  All families compute the
+ * same function.
  */
 int sbda_b200_set_kernel_path(int path);
 

@@ -21,7 +21,7 @@ from .norm_rope import norm_rope, rope_table
 from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_offsets
 
 __all__ = [
-    "PATH_TOPOLOGIES", "SBDAttention", "SBDAAttention", "device_status", "fused_sbda",
+    "BinaryPathAttention", "PATH_TOPOLOGIES", "SBDAttention", "SBDAAttention", "device_status", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
     "fused_sbda_key_backward", "host_offsets", "norm_rope", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
     "sbda_layer_offsets", "sbda_stage", "topology_offsets",
@@ -29,8 +29,8 @@ __all__ = [
 
 
 def __getattr__(name: str):
-    if name in ("SBDAttention", "SBDAAttention"):
-        from .attention import SBDAttention
+    if name in ("SBDAttention", "SBDAAttention", "BinaryPathAttention"):
+        from . import attention
 
-        return SBDAttention
+        return getattr(attention, name)
     raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

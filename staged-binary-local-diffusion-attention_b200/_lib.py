@@ -148,7 +148,8 @@ def offsets_array(offsets: tuple[int, ...]):
 
 
 def set_kernel_path(path: int) -> int:
-    """0 = automatic, 1 = general kernels only (process-wide); returns the previous value."""
+    """0 = automatic, 1 = general kernels (uniform ones where those cannot serve the offsets),
+    2 = uniform kernels only (process-wide); returns the previous value."""
     previous = load().sbda_b200_set_kernel_path(int(path))
     if previous < 0:
         raise ValueError(f"unknown kernel path {path}")

@@ -1,8 +1,9 @@
-"""``SBDAttention`` drop-in module running on the B200 kernels.
+"""``BinaryPathAttention`` / ``SBDAttention`` drop-in modules on the B200 kernels.
 
-Same constructor, state-dict keys (``q, k, v, out, q_norm.weight,
-k_norm.weight``) and ``forward`` signature as the reference module
-(``BiAttn/left_v2.py:100-198, 413-438``).  The fused route of the reference
+Same constructors, state-dict keys (``q, k, v, out, q_norm.weight,
+k_norm.weight``) and ``forward`` signature as the reference modules
+(``BiAttn/left_v2.py:100-198, 413-438``): ``BinaryPathAttention`` takes any
+path topology, ``SBDAttention`` is its ``topology="sbda"`` subclass.  The fused route of the reference
 (``left_v2.py:263-306``) is the only route here: inputs outside it -- CPU
 tensors, ``seam_reset``, caller path tables, masks with interior holes --
 raise instead of silently running another implementation.
@@ -35,18 +36,20 @@ class HeadRMSNorm(nn.Module):
         return (normalized * self.weight).to(dtype=x.dtype)
 
 
-class SBDAttention(nn.Module):
-    """Staged Binary-Local Diffusion Attention on the B200 kernels.
+class BinaryPathAttention(nn.Module):
+    """Causal exact-token attention over a selectable path topology (``left_v2.py:100-198``).
 
     ``use_sdpa``, ``use_fused`` and ``backward_mode`` are accepted for
-    signature compatibility (``left_v2.py:416-438``); every mode runs the
-    same deterministic gather-form kernels.  ``use_fused=False`` is refused:
-    the exact eager route is the reference's, not this package's.
+    signature compatibility; every mode runs the same deterministic
+    gather-form kernels.  ``use_fused=False`` is refused: the exact eager route
+    is the reference's, not this package's.  Layers whose topology has more
+    than four sources raise ``ValueError`` in ``forward``, as the reference's
+    fused ops do (``sbda_triton.py:1300-1302``).
     """
 
     def __init__(self, dim: int, heads: int, layer: int, *, kv_heads: int | None = None,
-                 rope_theta: float = 1_000_000.0, total_layers: int = 12, use_sdpa: bool = True,
-                 use_fused: bool = True, backward_mode: str = "key", topology: str = "sbda") -> None:
+                 rope_theta: float = 1_000_000.0, topology: str = "binary", total_layers: int = 12,
+                 use_sdpa: bool = True, use_fused: bool = True, backward_mode: str = "token") -> None:
         super().__init__()
         if dim <= 0 or heads <= 0 or dim % heads:
             raise ValueError("dim must be positive, heads must be positive, and divide dim")
@@ -57,7 +60,7 @@ class SBDAttention(nn.Module):
         if topology not in PATH_TOPOLOGIES:
             raise ValueError(f"unknown path topology: {topology}")
         if not use_fused:
-            raise ValueError("the B200 SBDA module only runs the fused route (use_fused=True)")
+            raise ValueError("the B200 attention modules only run the fused route (use_fused=True)")
         self.dim = int(dim)
         self.heads = int(heads)
         self.layer = int(layer)
@@ -115,6 +118,17 @@ class SBDAttention(nn.Module):
         if valid_mask is not None:
             out = out * valid_mask[:, :, None].to(dtype=out.dtype)
         return out
+
+
+class SBDAttention(BinaryPathAttention):
+    """Staged Binary-Local Diffusion Attention: the ``sbda`` topology (``left_v2.py:413-438``)."""
+
+    def __init__(self, dim: int, heads: int, layer: int, *, kv_heads: int | None = None,
+                 rope_theta: float = 1_000_000.0, total_layers: int = 12, use_sdpa: bool = True,
+                 use_fused: bool = True, backward_mode: str = "key") -> None:
+        super().__init__(dim, heads, layer, kv_heads=kv_heads, rope_theta=rope_theta, topology="sbda",
+                         total_layers=total_layers, use_sdpa=use_sdpa, use_fused=use_fused,
+                         backward_mode=backward_mode)
 
 
 SBDAAttention = SBDAttention

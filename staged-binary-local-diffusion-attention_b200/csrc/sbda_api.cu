@@ -27,7 +27,7 @@ unsigned* status_ptr() {
   return static_cast<unsigned*>(addr);
 }
 
-std::atomic<int> g_kernel_path{0};  // 0 = automatic, 1 = general kernels only
+std::atomic<int> g_kernel_path{0};  // 0 = automatic, 1 = general kernels, 2 = uniform kernels
 
 int sm_count() {
   int dev = 0, n = 148;
@@ -312,6 +312,45 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   return true;
 }
 
+// Plan of the uniform kernels (sbda_v3.cu): any offsets, each source its own
+// staged tile.  Tile height as in the windowed kernels (four rows per row group).
+bool plan_v3(int64_t D, int e, V3Plan* pl) {
+  const int pitch = row_pitch(D, e);
+  const int lane_bytes = e == 4 ? 32 : 16;
+  const int lpr = pitch / lane_bytes;
+  if (lpr != 4 && lpr != 8 && lpr != 16) return false;
+  if (lpr == 4 && e != 4) return false;
+  const size_t tile_bytes = (size_t)v2_tile(lpr) * pitch;
+  pl->lpr = lpr;
+  pl->tile = v2_tile(lpr);
+  pl->pitch = pitch;
+  pl->smem_fwd = (1 + 2 * 4) * tile_bytes + 16;  // sized for four sources
+  pl->smem_bwd = (2 + 2 * 4) * tile_bytes + 16;
+  return pl->smem_fwd <= kMaxSmem && pl->smem_bwd <= kMaxSmem;
+}
+
+void v3_params(V3Params* p, const sbda_shape& shape, const int32_t* off, int n, float scale, int tile) {
+  memset(p, 0, sizeof(*p));
+  p->B = (int)shape.batch;
+  p->H = (int)shape.heads;
+  p->Hkv = (int)shape.kv_heads;
+  p->G = (int)(shape.heads / shape.kv_heads);
+  p->L = (int)shape.length;
+  p->D = (int)shape.head_dim;
+  p->scale = scale;
+  p->S = n;
+  p->nT = (int)((shape.length + tile - 1) / tile);
+  p->o_min = off[0];
+  for (int s = 0; s < n; ++s) {
+    p->off[s] = off[s];
+    if (off[s] < p->o_min) {
+      p->o_min = off[s];
+      p->s_q = s;
+    }
+  }
+  p->status = status_ptr();
+}
+
 int validate(int dtype, const sbda_shape& s, const int32_t* off, int n) {
   if (dtype != SBDA_DTYPE_F32 && dtype != SBDA_DTYPE_F16 && dtype != SBDA_DTYPE_BF16) return SBDA_ERR_DTYPE;
   if (s.batch < 0 || s.heads < 0 || s.kv_heads < 0 || s.length < 0 || s.head_dim < 1) return SBDA_ERR_INVALID;
@@ -375,7 +414,7 @@ extern "C" const char* sbda_b200_status_string(int status) {
 }
 
 extern "C" int sbda_b200_set_kernel_path(int path) {
-  if (path != 0 && path != 1) return -1;
+  if (path < 0 || path > 2) return -1;
   return g_kernel_path.exchange(path);
 }
 
@@ -422,7 +461,24 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
   }
 
   Plan pl;
-  st = make_plan(offsets, n_offsets, L, D, e, &pl);
+  st = g_kernel_path.load() == 2 ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
+  if (st == SBDA_ERR_UNSUPPORTED) {  // several far offsets (or forced): the uniform kernels
+    V3Plan p3;
+    if (!plan_v3(D, e, &p3)) return SBDA_ERR_UNSUPPORTED;
+    V3Params p;
+    v3_params(&p, shape, offsets, n_offsets, scale, p3.tile);
+    p.q = arg_of(q);
+    p.k = arg_of(k);
+    p.v = arg_of(v);
+    p.out = arg_of(out);
+    p.lse = lse;
+    FwdMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    const bool tma = vec && encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p3.pitch, p3.tile) &&
+                     encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p3.pitch, p3.tile) &&
+                     encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p3.pitch, p3.tile);
+    return v3_forward(dtype, tma, maps, p, p3, s);
+  }
   if (st != SBDA_OK) return st;
   FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -513,7 +569,28 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
   }
 
   Plan pl;
-  st = make_plan(offsets, n_offsets, L, D, e, &pl);
+  st = g_kernel_path.load() == 2 ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
+  if (st == SBDA_ERR_UNSUPPORTED) {  // several far offsets (or forced): the uniform kernels
+    V3Plan p3;
+    if (!plan_v3(D, e, &p3)) return SBDA_ERR_UNSUPPORTED;
+    V3Params p;
+    v3_params(&p, shape, offsets, n_offsets, scale, p3.tile);
+    p.q = arg_of(q);
+    p.k = arg_of(k);
+    p.v = arg_of(v);
+    p.dout = arg_of(grad_out);
+    p.dq = arg_of(grad_q);
+    p.dk = arg_of(grad_k);
+    p.dv = arg_of(grad_v);
+    p.lse = const_cast<float*>(lse);
+    BwdMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    const bool tma = vec && encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p3.pitch, p3.tile) &&
+                     encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p3.pitch, p3.tile) &&
+                     encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p3.pitch, p3.tile) &&
+                     encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p3.pitch, p3.tile);
+    return v3_backward(dtype, tma, maps, p, p3, s);
+  }
   if (st != SBDA_OK) return st;
   BwdParams p;
   memset(&p, 0, sizeof(p));

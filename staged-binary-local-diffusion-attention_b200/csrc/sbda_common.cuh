@@ -601,6 +601,25 @@ struct BwdV2Params {
   int lse_box;   // rows of that box (Q/dO slot height rounded up to 32)
 };
 
+// Uniform kernels (sbda_v3.cu): every source a shifted tile.
+struct V3Params {
+  int B, H, Hkv, G, L, D;
+  float scale;
+  int S;
+  int off[4];
+  int nT;
+  int o_min, s_q;  // smallest offset and its source index (the dQ writer)
+  TensorArg q, k, v, out, dout, dq, dk, dv;
+  float* lse;      // forward writes, backward reads
+  unsigned slots_q, slots_k, slots_v, slots_d;
+  unsigned* status;
+};
+
+struct V3Plan {
+  int lpr, tile, pitch;
+  size_t smem_fwd, smem_bwd;
+};
+
 // v2 tile height for a row pitch: each of the 128/LPR row groups owns a run of
 // four consecutive rows.
 __host__ __device__ constexpr int v2_tile(int lpr) { return 4 * (kThreads / lpr); }
@@ -634,6 +653,8 @@ struct V2Plan {
 };
 
 int v2_forward(int dtype, bool tma, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st);
+int v3_forward(int dtype, bool tma, const FwdMaps& maps, const V3Params& p, const V3Plan& pl, cudaStream_t st);
+int v3_backward(int dtype, bool tma, const BwdMaps& maps, const V3Params& p, const V3Plan& pl, cudaStream_t st);
 int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
                 cudaStream_t st);
 

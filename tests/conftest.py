@@ -20,6 +20,9 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); parity tests through the C ABI")
 
 
+PATH_GOLDEN = os.path.join(ROOT, "tests", "golden", "path_golden.npz")
+
+
 class Golden:
     """Reference-generated vectors (see tests/golden/make_golden.py)."""
 
@@ -27,8 +30,8 @@ class Golden:
         self._data = np.load(path)
         meta = json.loads(bytes(self._data["manifest"]).decode())
         self.cases = meta["cases"]
-        self.schedules = meta["schedules"]
-        self.total_layers = meta["total_layers"]
+        self.schedules = meta.get("schedules", {})
+        self.total_layers = meta.get("total_layers", 12)
 
     def get(self, case: str, key: str):
         import torch
@@ -39,3 +42,8 @@ class Golden:
 @pytest.fixture(scope="session")
 def golden() -> Golden:
     return Golden(GOLDEN)
+
+
+@pytest.fixture(scope="session")
+def path_golden() -> Golden:
+    return Golden(PATH_GOLDEN)

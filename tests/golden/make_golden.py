@@ -17,7 +17,10 @@ and records, for seeded inputs:
   the above for a seeded upstream gradient,
 * the source schedule ``topology_offsets(l, topology)`` for layers 1..24.
 
-The output is ``tests/golden/sbda_golden.npz`` (float32, a few hundred KB).
+The output is ``tests/golden/sbda_golden.npz`` (float32, a few hundred KB),
+plus ``tests/golden/path_golden.npz``: ``BinaryPathAttention`` modules of
+other path topologies (module input, parameters, output, input gradient and
+parameter gradients; ``PATH_CASES``).
 The fixture never travels with a need for the reference: the GPU tests and
 the oracle tests only read the ``.npz``.
 """
@@ -46,6 +49,21 @@ CASES = [
     ("b2_len17_l4", 2, 17, 32, 2, 4),
     ("b2_len150_l8", 2, 150, 32, 2, 8),
     ("len160_l7_d64", 1, 160, 64, 1, 7),
+]
+
+# (name, batch, length, dim, heads, kv_heads, layer, topology): schedules served
+# by the windowed, general and uniform kernels (several far offsets), a
+# three-source layer and a GQA module.
+PATH_CASES = [
+    ("butterfly_l8", 1, 600, 32, 2, 2, 8, "butterfly"),
+    ("radix4_l4", 2, 200, 32, 2, 2, 4, "radix4"),
+    ("mesh_l8", 1, 300, 48, 3, 3, 8, "mesh"),
+    ("h2_l7", 1, 260, 32, 2, 2, 7, "h2"),
+    ("h8a_l5", 2, 40, 32, 4, 4, 5, "h8a"),
+    ("binary_l3", 1, 70, 32, 2, 2, 3, "binary"),
+    ("h5_l1", 1, 30, 16, 2, 2, 1, "h5"),
+    ("h6_l6", 1, 200, 32, 2, 2, 6, "h6"),
+    ("butterfly_gqa_l7", 1, 300, 64, 4, 2, 7, "butterfly"),
 ]
 
 TOPOLOGIES = ("sbda", "h8", "h8a", "h8b", "h8c", "h8d", "h8e", "binary", "h0", "h1",
@@ -130,6 +148,34 @@ def main() -> None:
                                                    "total_layers": 12}).encode(), dtype=np.uint8)
     np.savez_compressed(args.out, **arrays)
     print(f"wrote {args.out}: {len(manifest)} cases, {sum(a.nbytes for a in arrays.values())} bytes")
+
+    path_arrays: dict[str, np.ndarray] = {}
+    path_manifest = []
+    for name, batch, length, dim, heads, kv_heads, layer, topology in PATH_CASES:
+        torch.manual_seed(4321 + layer * 11 + length)
+        attn = left_v2.BinaryPathAttention(dim, heads, layer, kv_heads=kv_heads, topology=topology,
+                                           total_layers=12, use_fused=False)
+        with torch.no_grad():
+            attn.q_norm.weight.uniform_(0.5, 1.5)
+            attn.k_norm.weight.uniform_(0.5, 1.5)
+        x = torch.randn(batch, length, dim, requires_grad=True)
+        y = attn(x)
+        grad_y = torch.randn_like(y)
+        y.backward(grad_y)
+        record = {"x": x.detach(), "y": y.detach(), "grad_y": grad_y, "dx": x.grad}
+        for key, param in attn.state_dict().items():
+            record["param." + key] = param.detach()
+        for key, param in attn.named_parameters():
+            record["grad." + key] = param.grad.detach()
+        for key, value in record.items():
+            path_arrays[f"{name}/{key}"] = value.contiguous().to(torch.float32).numpy()
+        path_manifest.append({"name": name, "batch": batch, "length": length, "dim": dim, "heads": heads,
+                              "kv_heads": kv_heads, "layer": layer, "topology": topology,
+                              "offsets": list(topology_offsets(layer, topology=topology, total_layers=12))})
+    path_arrays["manifest"] = np.frombuffer(json.dumps({"cases": path_manifest}).encode(), dtype=np.uint8)
+    path_out = os.path.join(os.path.dirname(args.out), "path_golden.npz")
+    np.savez_compressed(path_out, **path_arrays)
+    print(f"wrote {path_out}: {len(path_manifest)} cases")
 
 
 if __name__ == "__main__":

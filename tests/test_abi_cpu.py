@@ -73,11 +73,19 @@ def test_forward_validation_codes(lib):
     assert _call_forward(lib, shape=(1, 3, 2, 64, 64)) == _lib.SBDA_ERR_INVALID
     assert _call_forward(lib, shape=(1, 2, 2, 64, 0)) == _lib.SBDA_ERR_INVALID
     assert _call_forward(lib, ptr=0) == _lib.SBDA_ERR_INVALID
-    # Two offsets beyond every tile height need two far tiles: outside the envelope.
-    assert _call_forward(lib, shape=(1, 2, 2, 10000, 64), offsets=(0, 1000, 3000)) == _lib.SBDA_ERR_UNSUPPORTED
+    # Sequences beyond 2^30 positions are outside the envelope.
+    assert _call_forward(lib, shape=(1, 2, 2, (1 << 30) + 1, 64)) == _lib.SBDA_ERR_UNSUPPORTED
     # Empty problems are a successful no-op (no device work).
     assert _call_forward(lib, shape=(0, 2, 2, 64, 64)) == _lib.SBDA_OK
     assert _call_forward(lib, shape=(1, 2, 2, 0, 64)) == _lib.SBDA_OK
+
+
+def test_kernel_path_values(lib):
+    assert _lib.set_kernel_path(2) == 0
+    assert _lib.set_kernel_path(1) == 2
+    assert _lib.set_kernel_path(0) == 1
+    with pytest.raises(ValueError):
+        _lib.set_kernel_path(3)
 
 
 def test_backward_validation_codes(lib):

@@ -20,10 +20,10 @@ from sbda_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["auto", "general"])
+@pytest.fixture(params=["auto", "general", "uniform"])
 def kernel_path(request):
-    """Runs a test through the windowed kernels (auto) and the general ones."""
-    previous = _lib.set_kernel_path(0 if request.param == "auto" else 1)
+    """Runs a test through the windowed kernels (auto), the general ones and the uniform ones."""
+    previous = _lib.set_kernel_path({"auto": 0, "general": 1, "uniform": 2}[request.param])
     yield request.param
     _lib.set_kernel_path(previous)
 
@@ -296,3 +296,38 @@ def test_local_carry_offsets(length, kernel_path):
     lower occupancy), with and without near offsets, across segment boundaries and ragged ends."""
     for offsets in ((0, 1, 2, 4), (0, 1, 2, 12), (0, 1, 2, 32), (0, 1, 2, 60), (0, 2, 48), (0, 8), (0, 1, 2, 6)):
         _check(1, 4, length, 64, torch.bfloat16, offsets, seed=length + offsets[-1])
+
+
+@pytest.mark.parametrize("length", [1, 65, 700, 3000])
+def test_several_far_offsets(length):
+    """Offset sets with more than one source beyond the tile (butterfly, radix-4, mesh and h2/h6
+    shapes at large strides, topology.py:102-145) and sets without a self source."""
+    for offsets in ((0, 64, 128, 192), (0, 1, 300, 301), (0, 129, 259), (50, 150), (0, 3, 9, 27),
+                    (64, 0, 128), (0, 256, 512, 768)):
+        _check(1, 2, length, 64, torch.bfloat16, offsets, seed=length + offsets[-1])
+    _check(1, 4, length, 40, torch.float32, (0, 100, 300, 301), kv_heads=2, layout="bhld", seed=length)
+    _check(2, 4, length, 128, torch.float16, (0, 65, 130), kv_heads=1, seed=length + 1)
+
+
+def test_path_topology_modules_match_reference_golden(path_golden):
+    """BinaryPathAttention over other topologies (butterfly, radix4, mesh, h2, h8a, binary, the
+    three-source h5 layer, GQA) reproduces the reference module: output, dx and parameter grads."""
+    for case in path_golden.cases:
+        name = case["name"]
+        module = sbda_b200.BinaryPathAttention(case["dim"], case["heads"], case["layer"],
+                                               kv_heads=case["kv_heads"], topology=case["topology"],
+                                               total_layers=12).cuda()
+        assert list(module.offsets) == case["offsets"]
+        state = {key[len("param."):]: path_golden.get(name, key) for key in
+                 ("param.q.weight", "param.k.weight", "param.v.weight", "param.out.weight",
+                  "param.q_norm.weight", "param.k_norm.weight")}
+        module.load_state_dict(state)
+        x = path_golden.get(name, "x").cuda().requires_grad_()
+        y = module(x)
+        y.backward(path_golden.get(name, "grad_y").cuda())
+        tol = dict(rtol=2e-5, atol=2e-5)
+        torch.testing.assert_close(y.detach().cpu(), path_golden.get(name, "y"), **tol, msg=name)
+        torch.testing.assert_close(x.grad.cpu(), path_golden.get(name, "dx"), **tol, msg=name)
+        for pname, param in module.named_parameters():
+            torch.testing.assert_close(param.grad.cpu(), path_golden.get(name, "grad." + pname), **tol,
+                                       msg=f"{name} {pname}")

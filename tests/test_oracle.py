@@ -109,3 +109,30 @@ def test_sampled_row_oracle_agrees_with_full_oracle():
     torch.testing.assert_close(dq_rows, dq[:, :, rows])
     torch.testing.assert_close(dk_rows, dk[:, :, rows])
     torch.testing.assert_close(dv_rows, dv[:, :, rows])
+
+
+def test_every_topology_matches_reference_table():
+    """All 31 path topologies against the reference's own schedules (tests/golden/topology_table.json,
+    written by tests/golden/make_topology_table.py from BiAttn/topology.py)."""
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(__file__), "golden", "topology_table.json")) as handle:
+        table = json.load(handle)
+    assert tuple(table["topologies"]) == sbda_b200.PATH_TOPOLOGIES
+    checked = 0
+    for name, by_total in table["offsets"].items():
+        for total, rows in by_total.items():
+            for layer, expected in zip(table["layers"], rows):
+                if expected is None:  # more than 64 offsets (h3 at large layers)
+                    continue
+                got = sbda_b200.topology_offsets(layer, topology=name, total_layers=int(total))
+                assert list(got) == expected, (name, total, layer)
+                checked += 1
+    assert checked > 1900  # 31 topologies x 22 layers x 3 stack depths, less the capped h3 rows
+
+
+def test_path_golden_offsets_match_topologies(path_golden):
+    for case in path_golden.cases:
+        assert list(sbda_b200.topology_offsets(case["layer"], topology=case["topology"], total_layers=12)) \
+            == case["offsets"], case["name"]
