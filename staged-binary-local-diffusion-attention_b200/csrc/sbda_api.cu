@@ -240,6 +240,35 @@ size_t bwd_smem(const V2Geometry& g, int T, int pitch) {
 // SM (228 KB per SM, 1 KB reserved per CTA).
 constexpr size_t kSmemThreeCtas = 228 * 1024 / 3 - 1024;
 
+// Segment length for `chains` walks of `len` tiles each on `slots` resident
+// CTAs.  Among splits that give at least 3.5 waves of CTAs (so the block
+// scheduler can even out CTAs that run long), minimise (waves, rounded up) x
+// (steps per CTA); a segment that is not the top of its walk first runs a
+// carry-only tile when `pre` is set, so segments are at least four tiles then.
+// Problems too small for 3.5 waves take the split with the most CTAs.
+int balanced_segment(int64_t chains, int len, bool pre, int64_t slots) {
+  int best = len;
+  bool best_full = false;
+  int64_t best_cost = 0, best_ctas = 0;
+  for (int segs = 1; segs <= len && segs <= 8192; ++segs) {
+    const int seg = (len + segs - 1) / segs;
+    if (pre && seg < 4 && segs > 1) break;
+    const int n_seg = (len + seg - 1) / seg;
+    if (n_seg != segs) continue;  // same split as a smaller count
+    const int64_t ctas = chains * n_seg;
+    const bool full = 2 * ctas >= 7 * slots;
+    const int64_t cost = (ctas + slots - 1) / slots * (seg + (pre && n_seg > 1 ? 1 : 0));
+    const bool better = full ? (!best_full || cost < best_cost) : (!best_full && ctas > best_ctas);
+    if (segs == 1 || better) {
+      best = seg;
+      best_full = full;
+      best_cost = cost;
+      best_ctas = ctas;
+    }
+  }
+  return best;
+}
+
 bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, int64_t B, int64_t H,
              V2Plan* pl) {
   if (G != 1) return false;
@@ -291,23 +320,13 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   pl->lse_box = lse_box_rows(g, T);
   pl->smem_bwd = bwd_smem(g, T, pitch);
   if (pl->smem_fwd > kMaxSmem || pl->smem_bwd > kMaxSmem) return false;
-  // Backward work split: about four CTAs' worth of tiles per resident slot.
-  const int64_t total = B * H * (int64_t)g.nT;
-  const int64_t target = (int64_t)sm_count() * 3 * 4;
-  int seg = (int)((total + target - 1) / target);
-  if (seg < 1) seg = 1;
-  // Chain and local-carry walks open with a carry-only tile: at least four tiles per walk.
-  if (g.mode != 1 && seg < 4) seg = 4;
-  if (g.mode == 0) {
-    if (seg >= g.A) seg = g.A;
-    g.seg = seg;
-    g.segs = (g.A + seg - 1) / seg;
-    pl->blocks_bwd = (unsigned)(B * H * (int64_t)g.R * g.segs);
-  } else {
-    g.seg = seg;
-    g.segs = (g.nT + seg - 1) / seg;
-    pl->blocks_bwd = (unsigned)(B * H * (int64_t)g.segs);
-  }
+  // Backward work split: walks of `chains` x `len` tiles cut into segments,
+  // one CTA each.
+  const int64_t chains = g.mode == 0 ? B * H * (int64_t)g.R : B * H;
+  const int len = g.mode == 0 ? g.A : g.nT;
+  g.seg = balanced_segment(chains, len, g.mode != 1, (int64_t)sm_count() * 3);
+  g.segs = (len + g.seg - 1) / g.seg;
+  pl->blocks_bwd = (unsigned)(chains * g.segs);
   pl->g = g;
   return true;
 }

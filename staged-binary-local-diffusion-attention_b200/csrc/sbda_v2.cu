@@ -304,16 +304,18 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
   // ---- Work assignment: a walk of tiles for this CTA. ----
   // Heads vary fastest across consecutive CTAs: the rows of all heads of a
   // position share DRAM pages and L2 lines in the [B, L, H, D] layout, so
-  // the heads of one walk segment run side by side.
+  // the heads of one walk segment run side by side.  Chains (residues r) vary
+  // next, before segments: neighbouring chains then walk side by side, and the
+  // 2-row halos a step reads from the adjacent tiles (another chain's) are in L2.
   int bid = blockIdx.x;
   int b, h, t_first, n_steps, stride, pre;
   h = bid % p.H;
   bid /= p.H;
   if (chain) {
-    const int s = bid % g.segs;
-    bid /= g.segs;
     const int r = bid % g.R;
-    b = bid / g.R;
+    bid /= g.R;
+    const int s = bid % g.segs;
+    b = bid / g.segs;
     const int A_r = (g.nT - 1 - r) / g.R + 1;
     const int a_lo = s * g.seg;
     if (a_lo >= A_r) return;
