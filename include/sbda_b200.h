@@ -184,6 +184,24 @@ int sbda_b200_norm_rope_backward_noalloc(int dtype, sbda_shape shape, sbda_tenso
                                          sbda_tensor grad_x, float* grad_weight, void* stream);
 
 /*
+ * Forward / backward with a per-row source mask, for rows whose usable sources
+ * depend on the data: padding holes and segment (seam) resets.
+ * source_mask[b * length + i], bit s set: source s of row i may be used (on
+ * top of i - offsets[s] >= 0).  A contiguous uint8 [batch, length] device
+ * array shared by all heads.  A row with no usable source gives zero output
+ * and zero gradients.  No counterpart in the reference: it builds the same
+ * per-row source validity inside its eager path (BiAttn/left_v2.py:349-373)
+ * and never calls its fused op there.  Runs on the uniform kernels.
+ */
+int sbda_b200_forward_masked(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                             float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                             const uint8_t* source_mask, sbda_tensor out, float* lse, void* stream);
+int sbda_b200_backward_masked(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                              float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                              const uint8_t* source_mask, sbda_tensor grad_out, const float* lse,
+                              sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v, void* stream);
+
+/*
  * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
  * (the windowed chain-walking kernels wherever they apply, else the general
  * ones, else the uniform ones), 1 = general kernels (uniform ones for offset

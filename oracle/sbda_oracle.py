@@ -112,14 +112,37 @@ def path_tensors(length: int, offsets: Sequence[int]) -> tuple[Tensor, Tensor]:
     return indices, valid
 
 
+def source_usable(length: int, offsets: Sequence[int], valid_mask: Tensor | None,
+                  seam_reset: Tensor | None) -> Tensor:
+    """``source_valid`` ``[B, L, S]`` of the reference's eager path for the default
+    per-layer paths with a padding mask and/or segment resets (``left_v2.py:349-373``)."""
+    ref = valid_mask if valid_mask is not None else seam_reset
+    indices, base = path_tensors(length, offsets)
+    batch = ref.shape[0]
+    source_count = indices.shape[-1]
+    gather_index = indices.unsqueeze(0).expand(batch, -1, -1)
+    valid = base.unsqueeze(0).expand(batch, -1, -1).clone()
+    if valid_mask is not None:
+        valid &= valid_mask.unsqueeze(-1).expand(-1, -1, source_count).gather(1, gather_index)
+        if seam_reset is not None:
+            seg = seam_reset.to(torch.int64).cumsum(dim=1)
+            valid &= seg.unsqueeze(-1).expand(-1, -1, source_count).gather(1, gather_index) == seg[:, :, None]
+        valid[:, :, 0] |= ~valid_mask
+    elif seam_reset is not None:
+        seg = seam_reset.to(torch.int64).cumsum(dim=1)
+        valid &= seg.unsqueeze(-1).expand(-1, -1, source_count).gather(1, gather_index) == seg[:, :, None]
+    return valid
+
+
 def exact_attention(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int],
-                    *, use_sdpa: bool = True) -> Tensor:
+                    *, use_sdpa: bool = True, usable: Tensor | None = None) -> Tensor:
     """Exact SBDA attention on ``[B,H,L,D]`` tensors (any float dtype).
 
-    Restates ``left_v2.py:335-405`` for the all-valid default route
-    (no ``valid_mask``, ``seam_reset`` or caller path table).  ``use_sdpa``
-    selects the batched-matmul form (``:380-396``) or the elementwise form
-    (``:397-405``), both of which the reference keeps.
+    Restates ``left_v2.py:335-405``: the all-valid default route, or, with
+    ``usable`` (``[B, L, S]``, from :func:`source_usable`), the masked route of
+    rows with padding holes or segment resets.  ``use_sdpa`` selects the
+    batched-matmul form (``:380-396``) or the elementwise form (``:397-405``),
+    both of which the reference keeps.
     """
     batch, heads, length, head_dim = q.shape
     indices, source_valid = path_tensors(length, offsets)
@@ -127,7 +150,7 @@ def exact_attention(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int],
     idx = indices[None, None, :, :, None].expand(batch, heads, length, source_count, head_dim)
     source_k = k.unsqueeze(3).expand(batch, heads, length, source_count, head_dim).gather(2, idx)
     source_v = v.unsqueeze(3).expand(batch, heads, length, source_count, head_dim).gather(2, idx)
-    invalid = ~source_valid[None, None, :, :]
+    invalid = ~source_valid[None, None, :, :] if usable is None else ~usable[:, None, :, :]
     if use_sdpa:
         scores = torch.matmul(q.unsqueeze(-2), source_k.transpose(-1, -2)).squeeze(-2)
     else:

@@ -87,6 +87,17 @@ def load() -> ctypes.CDLL:
             SbdaTensor, SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
+        lib.sbda_b200_forward_masked.restype = c_int
+        lib.sbda_b200_forward_masked.argtypes = [
+            c_int, SbdaShape, i32p, c_int32, c_float,
+            SbdaTensor, SbdaTensor, SbdaTensor, c_void_p, SbdaTensor, c_void_p, c_void_p,
+        ]
+        lib.sbda_b200_backward_masked.restype = c_int
+        lib.sbda_b200_backward_masked.argtypes = [
+            c_int, SbdaShape, i32p, c_int32, c_float,
+            SbdaTensor, SbdaTensor, SbdaTensor, c_void_p, SbdaTensor, c_void_p,
+            SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
+        ]
         lib.sbda_b200_norm_rope_forward.restype = c_int
         lib.sbda_b200_norm_rope_forward.argtypes = [
             c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,

@@ -4,9 +4,11 @@ Same constructors, state-dict keys (``q, k, v, out, q_norm.weight,
 k_norm.weight``) and ``forward`` signature as the reference modules
 (``BiAttn/left_v2.py:100-198, 413-438``): ``BinaryPathAttention`` takes any
 path topology, ``SBDAttention`` is its ``topology="sbda"`` subclass.  The fused route of the reference
-(``left_v2.py:263-306``) is the only route here: inputs outside it -- CPU
-tensors, ``seam_reset``, caller path tables, masks with interior holes --
-raise instead of silently running another implementation.
+(``left_v2.py:263-306``) serves the plain case; padding masks with interior
+holes and ``seam_reset`` -- which the reference sends to its eager path --
+run on the same kernels with a per-row source mask (``source_mask`` below).
+CPU tensors and caller path tables (``path_indices``/``path_valid``) raise
+instead of silently running another implementation.
 """
 
 from __future__ import annotations
@@ -94,14 +96,17 @@ class BinaryPathAttention(nn.Module):
             raise ValueError(f"expected dim={self.dim}, got {dim}")
         if valid_mask is not None and (valid_mask.shape != (batch, length) or valid_mask.dtype != torch.bool):
             raise ValueError("valid_mask must be bool with input shape")
-        if seam_reset is not None or path_indices is not None or path_valid is not None:
-            raise NotImplementedError("seam_reset / path tables are not served by the B200 SBDA kernels")
+        if seam_reset is not None and (seam_reset.shape != (batch, length) or seam_reset.dtype != torch.bool):
+            raise ValueError("seam_reset must be bool with input shape")
+        if path_indices is not None or path_valid is not None:
+            raise NotImplementedError("caller path tables are not served by the B200 SBDA kernels")
         if not x.is_cuda:
             raise RuntimeError("the B200 SBDA module requires CUDA inputs")
-        # Prefix-mask precondition of the fused route (left_v2.py:258-262).
-        if valid_mask is not None and valid_mask.shape[1] >= 2:
-            if not bool(torch.all(~valid_mask[:, 1:] | valid_mask[:, :-1])):
-                raise NotImplementedError("valid_mask with interior holes is not served by the B200 SBDA kernels")
+        # A prefix mask (left_v2.py:258-262) never hides a source from a valid row
+        # (sources are earlier positions), so it only needs the output multiply.
+        holes = (valid_mask is not None and valid_mask.shape[1] >= 2
+                 and not bool(torch.all(~valid_mask[:, 1:] | valid_mask[:, :-1])))
+        mask = self.source_mask(valid_mask, seam_reset) if holes or seam_reset is not None else None
         q = self.q(x).view(batch, length, self.heads, self.head_dim)
         k = self.k(x).view(batch, length, self.kv_heads, self.head_dim)
         v = self.v(x).view(batch, length, self.kv_heads, self.head_dim)
@@ -112,12 +117,39 @@ class BinaryPathAttention(nn.Module):
         k = k.permute(0, 2, 1, 3)
         v = v.permute(0, 2, 1, 3)
         _check_inputs(q, k, v, self.offsets, gqa=self.kv_heads != self.heads, source_counts=(1, 2, 3, 4))
-        attended = _SBDAFunction.apply(q, k, v, self.offsets)
+        attended = _SBDAFunction.apply(q, k, v, self.offsets, mask)
         attended = attended.transpose(1, 2).reshape(batch, length, dim)
         out = self.out(attended)
         if valid_mask is not None:
             out = out * valid_mask[:, :, None].to(dtype=out.dtype)
         return out
+
+    def source_mask(self, valid_mask: Tensor | None, seam_reset: Tensor | None) -> Tensor:
+        """Per-row source bits (uint8 ``[B, L]``, bit s = source s usable), ``left_v2.py:349-373``.
+
+        Source s of row i is position ``i - o_s``: usable if it exists, is not padding,
+        and lies in row i's segment (segments restart where ``seam_reset`` is set).
+        Padded rows keep source 0, as in the reference; their outputs are zeroed by the
+        output mask either way.
+        """
+        ref = valid_mask if valid_mask is not None else seam_reset
+        batch, length = ref.shape
+        device = ref.device
+        positions = torch.arange(length, device=device)
+        offsets = torch.tensor(self.offsets, device=device)
+        sources = positions[:, None] - offsets[None, :]                       # [L, S]
+        usable = (sources >= 0)[None].expand(batch, -1, -1)                   # [B, L, S]
+        index = sources.clamp_min(0)
+        if valid_mask is not None:
+            usable = usable & valid_mask[:, index]
+        if seam_reset is not None:
+            segment = seam_reset.to(torch.int64).cumsum(dim=1)
+            usable = usable & (segment[:, index] == segment[:, :, None])
+        if valid_mask is not None:
+            usable = usable.clone()
+            usable[:, :, 0] |= ~valid_mask
+        weights = (1 << torch.arange(len(self.offsets), device=device)).to(torch.uint8)
+        return (usable.to(torch.uint8) * weights).sum(dim=-1).to(torch.uint8).contiguous()
 
 
 class SBDAttention(BinaryPathAttention):

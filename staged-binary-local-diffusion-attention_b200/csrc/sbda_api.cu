@@ -414,6 +414,59 @@ bool tensors_vector_ok(std::initializer_list<const sbda_tensor*> ts, int64_t B, 
   return true;
 }
 
+// Uniform-kernel calls (also the masked entry points).  Shapes and pointers
+// are validated by the caller; `vec` says whether every view suits TMA.
+int uniform_forward(int dtype, const sbda_shape& shape, const int32_t* offsets, int n, float scale,
+                    const sbda_tensor& q, const sbda_tensor& k, const sbda_tensor& v, const uint8_t* mask,
+                    const sbda_tensor& out, float* lse, bool vec, cudaStream_t stream) {
+  const int e = elem_size(dtype);
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  V3Plan p3;
+  if (!plan_v3(D, e, &p3)) return SBDA_ERR_UNSUPPORTED;
+  V3Params p;
+  v3_params(&p, shape, offsets, n, scale, p3.tile);
+  p.q = arg_of(q);
+  p.k = arg_of(k);
+  p.v = arg_of(v);
+  p.out = arg_of(out);
+  p.lse = lse;
+  p.mask = mask;
+  FwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const bool tma = vec && encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p3.pitch, p3.tile) &&
+                   encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p3.pitch, p3.tile) &&
+                   encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p3.pitch, p3.tile);
+  return v3_forward(dtype, tma, maps, p, p3, stream);
+}
+
+int uniform_backward(int dtype, const sbda_shape& shape, const int32_t* offsets, int n, float scale,
+                     const sbda_tensor& q, const sbda_tensor& k, const sbda_tensor& v, const uint8_t* mask,
+                     const sbda_tensor& grad_out, const float* lse, const sbda_tensor& grad_q,
+                     const sbda_tensor& grad_k, const sbda_tensor& grad_v, bool vec, cudaStream_t stream) {
+  const int e = elem_size(dtype);
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  V3Plan p3;
+  if (!plan_v3(D, e, &p3)) return SBDA_ERR_UNSUPPORTED;
+  V3Params p;
+  v3_params(&p, shape, offsets, n, scale, p3.tile);
+  p.q = arg_of(q);
+  p.k = arg_of(k);
+  p.v = arg_of(v);
+  p.dout = arg_of(grad_out);
+  p.dq = arg_of(grad_q);
+  p.dk = arg_of(grad_k);
+  p.dv = arg_of(grad_v);
+  p.lse = const_cast<float*>(lse);
+  p.mask = mask;
+  BwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const bool tma = vec && encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p3.pitch, p3.tile) &&
+                   encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p3.pitch, p3.tile) &&
+                   encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p3.pitch, p3.tile) &&
+                   encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p3.pitch, p3.tile);
+  return v3_backward(dtype, tma, maps, p, p3, stream);
+}
+
 }  // namespace sbda
 
 using namespace sbda;
@@ -481,23 +534,8 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
 
   Plan pl;
   st = g_kernel_path.load() == 2 ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
-  if (st == SBDA_ERR_UNSUPPORTED) {  // several far offsets (or forced): the uniform kernels
-    V3Plan p3;
-    if (!plan_v3(D, e, &p3)) return SBDA_ERR_UNSUPPORTED;
-    V3Params p;
-    v3_params(&p, shape, offsets, n_offsets, scale, p3.tile);
-    p.q = arg_of(q);
-    p.k = arg_of(k);
-    p.v = arg_of(v);
-    p.out = arg_of(out);
-    p.lse = lse;
-    FwdMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    const bool tma = vec && encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p3.pitch, p3.tile) &&
-                     encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p3.pitch, p3.tile) &&
-                     encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p3.pitch, p3.tile);
-    return v3_forward(dtype, tma, maps, p, p3, s);
-  }
+  if (st == SBDA_ERR_UNSUPPORTED)  // several far offsets (or forced): the uniform kernels
+    return uniform_forward(dtype, shape, offsets, n_offsets, scale, q, k, v, nullptr, out, lse, vec, s);
   if (st != SBDA_OK) return st;
   FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -589,27 +627,9 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
 
   Plan pl;
   st = g_kernel_path.load() == 2 ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
-  if (st == SBDA_ERR_UNSUPPORTED) {  // several far offsets (or forced): the uniform kernels
-    V3Plan p3;
-    if (!plan_v3(D, e, &p3)) return SBDA_ERR_UNSUPPORTED;
-    V3Params p;
-    v3_params(&p, shape, offsets, n_offsets, scale, p3.tile);
-    p.q = arg_of(q);
-    p.k = arg_of(k);
-    p.v = arg_of(v);
-    p.dout = arg_of(grad_out);
-    p.dq = arg_of(grad_q);
-    p.dk = arg_of(grad_k);
-    p.dv = arg_of(grad_v);
-    p.lse = const_cast<float*>(lse);
-    BwdMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    const bool tma = vec && encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p3.pitch, p3.tile) &&
-                     encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p3.pitch, p3.tile) &&
-                     encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p3.pitch, p3.tile) &&
-                     encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p3.pitch, p3.tile);
-    return v3_backward(dtype, tma, maps, p, p3, s);
-  }
+  if (st == SBDA_ERR_UNSUPPORTED)  // several far offsets (or forced): the uniform kernels
+    return uniform_backward(dtype, shape, offsets, n_offsets, scale, q, k, v, nullptr, grad_out, lse, grad_q,
+                            grad_k, grad_v, vec, s);
   if (st != SBDA_OK) return st;
   BwdParams p;
   memset(&p, 0, sizeof(p));
@@ -647,6 +667,39 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
             encode_map(&maps.vH, &dummy, v, dtype, B, Hkv, L, D, pl.pitch, pl.g.Hn);
   }
   return v1_backward(dtype, tma, maps, p, pl, s);
+}
+
+extern "C" int sbda_b200_forward_masked(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                        float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                        const uint8_t* source_mask, sbda_tensor out, float* lse, void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || L == 0) return SBDA_OK;
+  if (!q.data || !k.data || !v.data || !out.data || !lse || !source_mask) return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  const bool vec = tensors_vector_ok({&q, &k, &v, &out}, B, L, D, e, {H, Hkv, Hkv, H});
+  return uniform_forward(dtype, shape, offsets, n_offsets, scale, q, k, v, source_mask, out, lse, vec,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbda_b200_backward_masked(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                         float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                         const uint8_t* source_mask, sbda_tensor grad_out, const float* lse,
+                                         sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v,
+                                         void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || L == 0) return SBDA_OK;
+  if (!q.data || !k.data || !v.data || !grad_out.data || !lse || !grad_q.data || !grad_k.data ||
+      !grad_v.data || !source_mask)
+    return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  const bool vec = tensors_vector_ok({&q, &k, &v, &grad_out, &grad_q, &grad_k, &grad_v}, B, L, D, e,
+                                     {H, Hkv, Hkv, H, H, Hkv, Hkv});
+  return uniform_backward(dtype, shape, offsets, n_offsets, scale, q, k, v, source_mask, grad_out, lse, grad_q,
+                          grad_k, grad_v, vec, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sbda_b200_device_status(uint32_t* flags_out, int reset) {

@@ -611,6 +611,7 @@ struct V3Params {
   int o_min, s_q;  // smallest offset and its source index (the dQ writer)
   TensorArg q, k, v, out, dout, dq, dk, dv;
   float* lse;      // forward writes, backward reads
+  const uint8_t* mask;  // optional [B, L]: bit s of row i allows source s (null = all)
   unsigned slots_q, slots_k, slots_v, slots_d;
   unsigned* status;
 };

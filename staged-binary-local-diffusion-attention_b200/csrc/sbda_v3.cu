@@ -22,6 +22,9 @@
 //    dQ = 0.
 //  Each consumer softmax is formed once per source (S times), the price of
 //  serving arbitrary offset sets without cross-tile records.
+//  * An optional per-row source mask (uint8 [B, L], bit s allows source s of
+//    that row) restricts the sources further: padding holes and segment
+//    resets, as the reference's eager path builds them (left_v2.py:349-373).
 
 #include "sbda_common.cuh"
 
@@ -86,6 +89,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v3_kernel(const __grid_cons
   for (int i = 0; i < 4; ++i) {
     const int r = grp * 4 + i, pos = i0 + r;
     const Frag q = FragIO<TE>::load(Qs + r * P, l);
+    const unsigned allow = p.mask ? (pos < p.L ? p.mask[(long long)b * p.L + pos] : 0u) : 0xFu;
     float sc[4];
     float m = -INFINITY;
 #pragma unroll
@@ -93,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v3_kernel(const __grid_cons
       sc[s] = -INFINITY;
       if (s < S) {
         const float a = lane_group_sum<LPR>(frag_dot(q, FragIO<TE>::load(Ks + (s * T + r) * P, l)));
-        if (pos - p.off[s] >= 0) sc[s] = a * c1;  // log2 units
+        if (pos - p.off[s] >= 0 && ((allow >> s) & 1u)) sc[s] = a * c1;  // log2 units
       }
       m = fmaxf(m, sc[s]);
     }
@@ -194,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 2) sbda_bwd_v3_kernel(const __grid_c
         const int r = a + i, cpos = c0 + r;
         const bool inr = cpos < p.L;
         const float lq = inr ? lse[cpos] * kLog2e : 0.f;
+        const unsigned allow = p.mask ? (inr ? p.mask[(long long)b * p.L + cpos] : 0u) : 0xFu;
         const Frag qf = FragIO<TE>::load(Qc + r * P, l);
         const Frag df = FragIO<TE>::load(Dc + r * P, l);
         float pr[4], bv[4];
@@ -204,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 2) sbda_bwd_v3_kernel(const __grid_c
           if (u < S) {
             const float av = lane_group_sum<LPR>(frag_dot(qf, FragIO<TE>::load(Ks + (u * T + r) * P, l)));
             bv[u] = lane_group_sum<LPR>(frag_dot(df, FragIO<TE>::load(Vs + (u * T + r) * P, l)));
-            if (inr && cpos - p.off[u] >= 0) pr[u] = fast_exp2(fmaf(av, c1, -lq));
+            if (inr && cpos - p.off[u] >= 0 && ((allow >> u) & 1u)) pr[u] = fast_exp2(fmaf(av, c1, -lq));
             delta = fmaf(pr[u], bv[u], delta);
           }
         }

@@ -96,10 +96,21 @@ def _check_inputs(q: Tensor, k: Tensor, v: Tensor, offsets: tuple[int, ...], *, 
         raise ValueError("q, k and v must be on one device")
 
 
+def _check_source_mask(mask: Tensor, q: Tensor) -> None:
+    if mask.dtype != torch.uint8 or mask.shape != (q.shape[0], q.shape[2]) or not mask.is_contiguous():
+        raise ValueError("source_mask must be a contiguous uint8 [B, L] tensor")
+    if mask.device != q.device:
+        raise ValueError("source_mask must be on q's device")
+
+
 def sbda_forward(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int], *,
                  scale: float | None = None, out: Tensor | None = None,
-                 lse: Tensor | None = None) -> tuple[Tensor, Tensor]:
-    """Forward through the C ABI: returns ``(out, lse)``; ``lse`` is fp32 ``[B,H,L]``."""
+                 lse: Tensor | None = None, source_mask: Tensor | None = None) -> tuple[Tensor, Tensor]:
+    """Forward through the C ABI: returns ``(out, lse)``; ``lse`` is fp32 ``[B,H,L]``.
+
+    ``source_mask`` (optional, uint8 ``[B, L]``): bit s of row i allows source s of that row
+    (``sbda_b200_forward_masked``).
+    """
     offsets = tuple(int(o) for o in offsets)
     batch, heads, length, head_dim = q.shape
     if out is None:
@@ -111,18 +122,28 @@ def sbda_forward(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int], *,
     lib = _lib.load()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        status = lib.sbda_b200_forward(
-            _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
-            _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(out), lse.data_ptr(), stream,
-        )
+        if source_mask is None:
+            status = lib.sbda_b200_forward(
+                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+                _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(out), lse.data_ptr(), stream,
+            )
+        else:
+            _check_source_mask(source_mask, q)
+            status = lib.sbda_b200_forward_masked(
+                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+                _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), source_mask.data_ptr(), _tensor_arg(out),
+                lse.data_ptr(), stream,
+            )
     _lib.raise_for_status(status, "sbda_b200_forward")
     return out, lse
 
 
 def sbda_backward(q: Tensor, k: Tensor, v: Tensor, grad_out: Tensor, lse: Tensor,
                   offsets: Sequence[int], *, scale: float | None = None,
-                  grads: tuple[Tensor, Tensor, Tensor] | None = None) -> tuple[Tensor, Tensor, Tensor]:
-    """Backward through the C ABI: returns ``(dq, dk, dv)`` in the input dtype."""
+                  grads: tuple[Tensor, Tensor, Tensor] | None = None,
+                  source_mask: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    """Backward through the C ABI: returns ``(dq, dk, dv)`` in the input dtype (``source_mask`` as
+    in :func:`sbda_forward`)."""
     offsets = tuple(int(o) for o in offsets)
     if grad_out.dtype != q.dtype:
         grad_out = grad_out.to(q.dtype)
@@ -138,11 +159,19 @@ def sbda_backward(q: Tensor, k: Tensor, v: Tensor, grad_out: Tensor, lse: Tensor
     lib = _lib.load()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        status = lib.sbda_b200_backward(
-            _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
-            _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(grad_out), lse.data_ptr(),
-            _tensor_arg(dq), _tensor_arg(dk), _tensor_arg(dv), stream,
-        )
+        if source_mask is None:
+            status = lib.sbda_b200_backward(
+                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+                _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(grad_out), lse.data_ptr(),
+                _tensor_arg(dq), _tensor_arg(dk), _tensor_arg(dv), stream,
+            )
+        else:
+            _check_source_mask(source_mask, q)
+            status = lib.sbda_b200_backward_masked(
+                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+                _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), source_mask.data_ptr(), _tensor_arg(grad_out),
+                lse.data_ptr(), _tensor_arg(dq), _tensor_arg(dk), _tensor_arg(dv), stream,
+            )
     _lib.raise_for_status(status, "sbda_b200_backward")
     return dq, dk, dv
 
@@ -156,17 +185,19 @@ class _SBDAFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, offsets: tuple[int, ...]) -> Tensor:
-        out, lse = sbda_forward(q, k, v, offsets)
+    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, offsets: tuple[int, ...],
+                source_mask: Tensor | None = None) -> Tensor:
+        out, lse = sbda_forward(q, k, v, offsets, source_mask=source_mask)
         ctx.save_for_backward(q, k, v, lse)
         ctx.offsets = offsets
+        ctx.source_mask = source_mask
         return out
 
     @staticmethod
     def backward(ctx, grad_out: Tensor):
         q, k, v, lse = ctx.saved_tensors
-        dq, dk, dv = sbda_backward(q, k, v, grad_out, lse, ctx.offsets)
-        return dq, dk, dv, None
+        dq, dk, dv = sbda_backward(q, k, v, grad_out, lse, ctx.offsets, source_mask=ctx.source_mask)
+        return dq, dk, dv, None, None
 
 
 def _apply(q: Tensor, k: Tensor, v: Tensor, offsets: Tensor | Sequence[int], *, gqa: bool) -> Tensor:

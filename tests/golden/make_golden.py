@@ -66,6 +66,17 @@ PATH_CASES = [
     ("butterfly_gqa_l7", 1, 300, 64, 4, 2, 7, "butterfly"),
 ]
 
+# Modules with data-dependent source masks, run on the reference's eager path
+# (left_v2.py:349-373): (name, batch, length, dim, heads, kv_heads, layer,
+# topology, padding holes, segment resets, right padding).
+MASK_CASES = [
+    ("sbda_holes_l5", 2, 90, 32, 2, 2, 5, "sbda", True, False, 0),
+    ("sbda_seams_l4", 2, 100, 32, 2, 2, 4, "sbda", False, True, 0),
+    ("sbda_both_l6", 1, 120, 32, 2, 2, 6, "sbda", True, True, 9),
+    ("butterfly_seams_l7", 1, 300, 32, 2, 2, 7, "butterfly", False, True, 0),
+    ("sbda_gqa_holes_l3", 1, 80, 64, 4, 2, 3, "sbda", True, False, 5),
+]
+
 TOPOLOGIES = ("sbda", "h8", "h8a", "h8b", "h8c", "h8d", "h8e", "binary", "h0", "h1",
               "h7", "local_jump", "longformer_local")
 
@@ -171,6 +182,40 @@ def main() -> None:
             path_arrays[f"{name}/{key}"] = value.contiguous().to(torch.float32).numpy()
         path_manifest.append({"name": name, "batch": batch, "length": length, "dim": dim, "heads": heads,
                               "kv_heads": kv_heads, "layer": layer, "topology": topology,
+                              "offsets": list(topology_offsets(layer, topology=topology, total_layers=12))})
+    for name, batch, length, dim, heads, kv_heads, layer, topology, holes, seams, pad in MASK_CASES:
+        gen = torch.Generator().manual_seed(777 + layer * 13 + length)
+        valid_mask = torch.ones(batch, length, dtype=torch.bool)
+        if holes:
+            valid_mask &= torch.rand(batch, length, generator=gen) > 0.15
+        if pad:
+            valid_mask[:, length - pad:] = False
+        seam_reset = (torch.rand(batch, length, generator=gen) < 0.05) if seams else None
+        torch.manual_seed(99 + layer * 5 + length)
+        attn = left_v2.BinaryPathAttention(dim, heads, layer, kv_heads=kv_heads, topology=topology,
+                                           total_layers=12, use_fused=False)
+        with torch.no_grad():
+            attn.q_norm.weight.uniform_(0.5, 1.5)
+            attn.k_norm.weight.uniform_(0.5, 1.5)
+        x = torch.randn(batch, length, dim, requires_grad=True)
+        has_mask = holes or pad > 0
+        y = attn(x, valid_mask=valid_mask if has_mask else None, seam_reset=seam_reset)
+        grad_y = torch.randn_like(y)
+        y.backward(grad_y)
+        record = {"x": x.detach(), "y": y.detach(), "grad_y": grad_y, "dx": x.grad}
+        if has_mask:
+            record["valid_mask"] = valid_mask.to(torch.float32)
+        if seam_reset is not None:
+            record["seam_reset"] = seam_reset.to(torch.float32)
+        for key, param in attn.state_dict().items():
+            record["param." + key] = param.detach()
+        for key, param in attn.named_parameters():
+            record["grad." + key] = param.grad.detach()
+        for key, value in record.items():
+            path_arrays[f"{name}/{key}"] = value.contiguous().to(torch.float32).numpy()
+        path_manifest.append({"name": name, "batch": batch, "length": length, "dim": dim, "heads": heads,
+                              "kv_heads": kv_heads, "layer": layer, "topology": topology,
+                              "valid_mask": has_mask, "seam_reset": seam_reset is not None,
                               "offsets": list(topology_offsets(layer, topology=topology, total_layers=12))})
     path_arrays["manifest"] = np.frombuffer(json.dumps({"cases": path_manifest}).encode(), dtype=np.uint8)
     path_out = os.path.join(os.path.dirname(args.out), "path_golden.npz")

@@ -311,7 +311,8 @@ def test_several_far_offsets(length):
 
 def test_path_topology_modules_match_reference_golden(path_golden):
     """BinaryPathAttention over other topologies (butterfly, radix4, mesh, h2, h8a, binary, the
-    three-source h5 layer, GQA) reproduces the reference module: output, dx and parameter grads."""
+    three-source h5 layer, GQA), and modules with padding holes and segment resets (the
+    reference's eager route), reproduce the reference module: output, dx and parameter grads."""
     for case in path_golden.cases:
         name = case["name"]
         module = sbda_b200.BinaryPathAttention(case["dim"], case["heads"], case["layer"],
@@ -323,7 +324,9 @@ def test_path_topology_modules_match_reference_golden(path_golden):
                   "param.q_norm.weight", "param.k_norm.weight")}
         module.load_state_dict(state)
         x = path_golden.get(name, "x").cuda().requires_grad_()
-        y = module(x)
+        valid_mask = path_golden.get(name, "valid_mask").cuda().bool() if case.get("valid_mask") else None
+        seam_reset = path_golden.get(name, "seam_reset").cuda().bool() if case.get("seam_reset") else None
+        y = module(x, valid_mask=valid_mask, seam_reset=seam_reset)
         y.backward(path_golden.get(name, "grad_y").cuda())
         tol = dict(rtol=2e-5, atol=2e-5)
         torch.testing.assert_close(y.detach().cpu(), path_golden.get(name, "y"), **tol, msg=name)
@@ -331,3 +334,39 @@ def test_path_topology_modules_match_reference_golden(path_golden):
         for pname, param in module.named_parameters():
             torch.testing.assert_close(param.grad.cpu(), path_golden.get(name, "grad." + pname), **tol,
                                        msg=f"{name} {pname}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_source_masks_match_oracle(dtype):
+    """Per-row source masks (padding holes, segment resets) through sbda_b200_forward_masked /
+    sbda_b200_backward_masked against the oracle's masked route (left_v2.py:349-396)."""
+    g = torch.Generator().manual_seed(5)
+    for layer, length, kv_heads in ((3, 300, 4), (7, 700, 4), (10, 1500, 2), (2, 130, 4)):
+        offsets = sbda_b200.topology_offsets(layer)
+        q, k, v, do = _inputs(2, 4, length, 64, dtype, kv_heads=kv_heads, seed=layer)
+        valid_mask = torch.rand(2, length, generator=g) > 0.1
+        valid_mask[1, length - 17:] = False
+        seam_reset = torch.rand(2, length, generator=g) < 0.03
+        module = sbda_b200.BinaryPathAttention(32, 2, layer, topology="sbda")
+        for vm, sr in ((valid_mask, None), (None, seam_reset), (valid_mask, seam_reset)):
+            bits = module.source_mask(vm.cuda() if vm is not None else None,
+                                      sr.cuda() if sr is not None else None)
+            qq, kk, vv = (t.detach().requires_grad_() for t in (q, k, v))
+            out = sbda_b200.ops._SBDAFunction.apply(qq, kk, vv, offsets, bits)
+            out.backward(do)
+            usable = orc.source_usable(length, offsets, vm, sr)
+            group = 4 // kv_heads
+            qc, kc, vc, doc = (t.detach().cpu().double() for t in (q, k, v, do))
+            kc, vc = kc.repeat_interleave(group, 1), vc.repeat_interleave(group, 1)
+            qc, kc, vc = (t.requires_grad_() for t in (qc, kc, vc))
+            ref = orc.exact_attention(qc, kc, vc, offsets, usable=usable)
+            ref.backward(doc)
+            rdk = kc.grad.view(2, kv_heads, group, length, 64).sum(2)
+            rdv = vc.grad.view(2, kv_heads, group, length, 64).sum(2)
+            rows = usable.any(-1)  # rows with a usable source (others: zero output in both)
+            tag = f"layer {layer} {dtype} holes={vm is not None} seams={sr is not None}"
+            _close(out, ref.detach(), dtype, "O " + tag)
+            _close(qq.grad, qc.grad, dtype, "dQ " + tag)
+            _close(kk.grad, rdk, dtype, "dK " + tag, rtol=2.0 ** -8 if dtype != torch.float32 else None)
+            _close(vv.grad, rdv, dtype, "dV " + tag, rtol=2.0 ** -8 if dtype != torch.float32 else None)
+            assert bool(rows.any())
