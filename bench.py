@@ -42,7 +42,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("cfg4", "cfg5"), default="cfg4",
+    p.add_argument("--workload", choices=("cfg4", "cfg5", "block"), default="cfg4",
                    help="cfg4 (default, the metric): one 1M-position sequence per GPU; cfg5: one "
                         "4M-position, 22-layer sequence split into contiguous shards across the GPUs")
     p.add_argument("--length", type=int, default=1 << 20)
@@ -472,12 +472,88 @@ def run_seqshard(args) -> None:
         dist.destroy_process_group()
 
 
+def run_block(args) -> None:
+    """Block parts around the attention op (BiAttn/model.py:299-335) at the config-4 width.
+
+    Times, per layer, the forward and backward of everything in the block that is neither a GEMM
+    nor the attention op: the pre-attention RMSNorm, the attention's padding-row multiply, the
+    residual add, the pre-FFN RMSNorm, the SwiGLU gate and the final masked residual.  Two arms on
+    the same seeded inputs: the reference's eager ops and this package's fused kernels.  One
+    JSON line; the fused arm's algorithmic bytes give its HBM roofline.
+    """
+    import torch.nn.functional as F
+
+    from sbda_b200 import block as blk
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L, dim, hidden = args.length, args.heads * args.head_dim, 4 * args.heads * args.head_dim
+    dtype = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(77)
+    mk = lambda *s: torch.randn(*s, device=dev, generator=g).to(dtype)  # noqa: E731
+    x, attn_out, ff = mk(1, L, dim), mk(1, L, dim), mk(1, L, dim)
+    gate, up = mk(1, L, hidden), mk(1, L, hidden)
+    mask = torch.rand(1, L, device=dev, generator=g) > 0.01
+    w1, w2 = (torch.rand(dim, device=dev, generator=g) + 0.5 for _ in range(2))
+    dys = [mk(1, L, dim), mk(1, L, dim), mk(1, L, hidden)]  # gradients reaching n1, y, h
+
+    def eager():
+        xs, a, gt, u, f = (t.detach().requires_grad_() for t in (x, attn_out, gate, up, ff))
+        n1 = F.rms_norm(xs, (dim,), w1.to(dtype), 1e-6)
+        x1 = xs + a * mask[:, :, None].to(dtype)
+        n2 = F.rms_norm(x1, (dim,), w2.to(dtype), 1e-6)
+        h = F.silu(gt) * u
+        y = x1 + f * mask[:, :, None].to(dtype)
+        torch.autograd.backward((n1, y, h, n2), (dys[0], dys[1], dys[2], dys[0]))
+
+    def fused():
+        xs, a, gt, u, f = (t.detach().requires_grad_() for t in (x, attn_out, gate, up, ff))
+        n1 = blk.rms_norm(xs, w1)
+        x1, n2 = blk.add_rms_norm(xs, a, w2, 1e-6, mask)
+        h = blk.silu_mul(gt, u)
+        y = torch.addcmul(x1, f, mask[:, :, None].to(dtype))
+        torch.autograd.backward((n1, y, h, n2), (dys[0], dys[1], dys[2], dys[0]))
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / args.steps
+
+    eager_ms, fused_ms = timed(eager), timed(fused)
+    e, r = 2, L
+    # Fused arm, algorithmic bytes (each tensor read or written once per kernel):
+    # fwd norm1 x->n1 (2), add+norm x,a->x1,n2 (4), gate g,u->h (3h), residual x1,f->y (3);
+    # bwd norm1 x,dn1->dx (3), add+norm x1,dn2,dy->dx,da (5), gate g,u,dh->dg,du (5h), residual dy->df (2).
+    units = (2 + 4 + 3 + 3 + 5 + 2) * dim + (3 + 5) * hidden
+    algo = r * e * units + r * (4 * 4 + 1 * 2)  # + rstd rows, mask bytes
+    achieved = algo / (fused_ms * 1e-3) / 1e9
+    peak, _ = measured_peak_gbs()
+    print(json.dumps({
+        "metric": "SBDA block elementwise parts (norms, residuals, masks, SwiGLU gate) fwd+bwd ms per layer",
+        "value": fused_ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "higher_is_better": False, "eager_ms": eager_ms, "speedup_vs_eager": eager_ms / fused_ms,
+        "dtype": "bf16", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "block parts at config 4 width", "positions": L, "dim": dim, "ffn_hidden": hidden},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "algorithmic_bytes": algo},
+    }), flush=True)
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "cfg5":
         run_seqshard(args)
+    elif args.workload == "block":
+        run_block(args)
     else:
         run_b200(args)
 

@@ -202,6 +202,47 @@ int sbda_b200_backward_masked(int dtype, sbda_shape shape, const int32_t* offset
                               sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v, void* stream);
 
 /*
+ * Block parts around the attention op (BiAttn/model.py:299-335).  No C
+ * counterpart in the reference, which runs them as eager torch ops
+ * (RMSNorm model.py:25-29, residual add model.py:325, SwiGLU gate
+ * model.py:58-59, padding-row mask left_v2.py:404).  Rows are contiguous
+ * [rows, dim] arrays in the dtype, 16-byte aligned; dim % 8 == 0, dim <= 2048.
+ *
+ * Residual + row mask + RMSNorm: x1 = x + m * residual_add (when residual_add
+ * is non-null; m = row_mask[row] != 0, all rows if row_mask is null; x1 is
+ * rounded to the dtype and written to x1_out), y = x1 * rsqrt(mean(x1^2) +
+ * eps) * weight; rstd[row] = that rsqrt (fp32, saved for the backward).
+ * weight is fp32 [dim].
+ */
+int sbda_b200_rms_norm_forward(int dtype, int64_t rows, int64_t dim, const void* x,
+                               const void* residual_add, const uint8_t* row_mask,
+                               const float* weight, float eps, void* x1_out, void* y,
+                               float* rstd, void* stream);
+
+/* fp32 workspace floats the norm backward needs for `rows` x `dim`. */
+int64_t sbda_b200_rms_norm_workspace_floats(int64_t rows, int64_t dim);
+
+/*
+ * Backward of the above: grad_x = d/dx1 (norm part) + grad_x1 (a gradient that
+ * reaches x1 from elsewhere, nullable), grad_residual = m * grad_x (nullable),
+ * grad_weight = fp32 [dim], summed over rows in a fixed order (deterministic).
+ */
+int sbda_b200_rms_norm_backward(int dtype, int64_t rows, int64_t dim, const void* x1,
+                                const float* rstd, const float* weight, const void* grad_y,
+                                const void* grad_x1, const uint8_t* row_mask, void* grad_x,
+                                void* grad_residual, float* grad_weight, float* workspace,
+                                int64_t workspace_floats, void* stream);
+
+/*
+ * SwiGLU gate over n elements (n % 8 == 0): h = silu(gate) * up, each op rounded
+ * to the dtype as eager torch runs them; backward writes grad_gate, grad_up.
+ */
+int sbda_b200_silu_mul_forward(int dtype, int64_t n, const void* gate, const void* up, void* h,
+                               void* stream);
+int sbda_b200_silu_mul_backward(int dtype, int64_t n, const void* gate, const void* up,
+                                const void* grad_h, void* grad_gate, void* grad_up, void* stream);
+
+/*
  * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
  * (the windowed chain-walking kernels wherever they apply, else the general
  * ones, else the uniform ones), 1 = general kernels (uniform ones for offset

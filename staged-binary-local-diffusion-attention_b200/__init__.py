@@ -21,7 +21,8 @@ from .norm_rope import norm_rope, rope_table
 from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_offsets
 
 __all__ = [
-    "BinaryPathAttention", "PATH_TOPOLOGIES", "SBDAttention", "SBDAAttention", "device_status", "fused_sbda",
+    "BiAttnBlock", "BinaryPathAttention", "PATH_TOPOLOGIES", "RMSNorm", "SBDAttention", "SwiGLU",
+    "add_rms_norm", "rms_norm", "silu_mul", "SBDAAttention", "device_status", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
     "fused_sbda_key_backward", "host_offsets", "norm_rope", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
     "sbda_layer_offsets", "sbda_stage", "topology_offsets",
@@ -33,4 +34,8 @@ def __getattr__(name: str):
         from . import attention
 
         return getattr(attention, name)
+    if name in ("BiAttnBlock", "RMSNorm", "SwiGLU", "add_rms_norm", "rms_norm", "silu_mul"):
+        from . import block
+
+        return getattr(block, name)
     raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

@@ -98,6 +98,25 @@ def load() -> ctypes.CDLL:
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p, SbdaTensor, c_void_p,
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
+        u8p = c_void_p
+        lib.sbda_b200_rms_norm_forward.restype = c_int
+        lib.sbda_b200_rms_norm_forward.argtypes = [
+            c_int, ctypes.c_int64, ctypes.c_int64, c_void_p, c_void_p, u8p, c_void_p, c_float,
+            c_void_p, c_void_p, c_void_p, c_void_p,
+        ]
+        lib.sbda_b200_rms_norm_workspace_floats.restype = ctypes.c_int64
+        lib.sbda_b200_rms_norm_workspace_floats.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        lib.sbda_b200_rms_norm_backward.restype = c_int
+        lib.sbda_b200_rms_norm_backward.argtypes = [
+            c_int, ctypes.c_int64, ctypes.c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, u8p,
+            c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_int64, c_void_p,
+        ]
+        lib.sbda_b200_silu_mul_forward.restype = c_int
+        lib.sbda_b200_silu_mul_forward.argtypes = [c_int, ctypes.c_int64, c_void_p, c_void_p, c_void_p, c_void_p]
+        lib.sbda_b200_silu_mul_backward.restype = c_int
+        lib.sbda_b200_silu_mul_backward.argtypes = [
+            c_int, ctypes.c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+        ]
         lib.sbda_b200_norm_rope_forward.restype = c_int
         lib.sbda_b200_norm_rope_forward.argtypes = [
             c_int, SbdaShape, SbdaTensor, SbdaTensor, c_void_p, c_float, c_void_p, c_void_p,

@@ -89,6 +89,15 @@ class BinaryPathAttention(nn.Module):
 
     def forward(self, x: Tensor, valid_mask: Tensor | None = None, seam_reset: Tensor | None = None,
                 path_indices: Tensor | None = None, path_valid: Tensor | None = None) -> Tensor:
+        out = self._attend(x, valid_mask, seam_reset, path_indices, path_valid)
+        if valid_mask is not None:
+            out = out * valid_mask[:, :, None].to(dtype=out.dtype)
+        return out
+
+    def _attend(self, x: Tensor, valid_mask: Tensor | None = None, seam_reset: Tensor | None = None,
+                path_indices: Tensor | None = None, path_valid: Tensor | None = None) -> Tensor:
+        """``forward`` without the final padding-row multiply (a caller that fuses it, the
+        block, applies it)."""
         if x.ndim != 3:
             raise ValueError("x must have shape [batch, sequence, dim]")
         batch, length, dim = x.shape
@@ -119,10 +128,7 @@ class BinaryPathAttention(nn.Module):
         _check_inputs(q, k, v, self.offsets, gqa=self.kv_heads != self.heads, source_counts=(1, 2, 3, 4))
         attended = _SBDAFunction.apply(q, k, v, self.offsets, mask)
         attended = attended.transpose(1, 2).reshape(batch, length, dim)
-        out = self.out(attended)
-        if valid_mask is not None:
-            out = out * valid_mask[:, :, None].to(dtype=out.dtype)
-        return out
+        return self.out(attended)
 
     def source_mask(self, valid_mask: Tensor | None, seam_reset: Tensor | None) -> Tensor:
         """Per-row source bits (uint8 ``[B, L]``, bit s = source s usable), ``left_v2.py:349-373``.

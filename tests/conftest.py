@@ -21,6 +21,7 @@ def pytest_configure(config):
 
 
 PATH_GOLDEN = os.path.join(ROOT, "tests", "golden", "path_golden.npz")
+BLOCK_GOLDEN = os.path.join(ROOT, "tests", "golden", "block_golden.npz")
 
 
 class Golden:
@@ -47,3 +48,8 @@ def golden() -> Golden:
 @pytest.fixture(scope="session")
 def path_golden() -> Golden:
     return Golden(PATH_GOLDEN)
+
+
+@pytest.fixture(scope="session")
+def block_golden() -> Golden:
+    return Golden(BLOCK_GOLDEN)

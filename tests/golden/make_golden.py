@@ -20,7 +20,8 @@ and records, for seeded inputs:
 The output is ``tests/golden/sbda_golden.npz`` (float32, a few hundred KB),
 plus ``tests/golden/path_golden.npz``: ``BinaryPathAttention`` modules of
 other path topologies (module input, parameters, output, input gradient and
-parameter gradients; ``PATH_CASES``).
+parameter gradients; ``PATH_CASES``), and ``tests/golden/block_golden.npz``:
+whole ``BiAttnBlock`` layers (``BLOCK_CASES``).
 The fixture never travels with a need for the reference: the GPU tests and
 the oracle tests only read the ``.npz``.
 """
@@ -75,6 +76,16 @@ MASK_CASES = [
     ("sbda_both_l6", 1, 120, 32, 2, 2, 6, "sbda", True, True, 9),
     ("butterfly_seams_l7", 1, 300, 32, 2, 2, 7, "butterfly", False, True, 0),
     ("sbda_gqa_holes_l3", 1, 80, 64, 4, 2, 3, "sbda", True, False, 5),
+]
+
+# Whole blocks (BiAttn/model.py:248-335): (name, batch, length, dim, heads,
+# kv_heads, layer_index, backend, topology, ff_hidden, ff_bias, mask kind).
+# Mask kinds: "none", "prefix" (right padding), "holes_seams".
+BLOCK_CASES = [
+    ("block_sbda_l3_prefix", 2, 48, 64, 4, None, 2, "sbda", "binary", None, False, "prefix"),
+    ("block_sbda_gqa_l6_holes", 1, 100, 128, 4, 2, 5, "sbda", "binary", 192, True, "holes_seams"),
+    ("block_leftv2_butterfly_l8", 1, 300, 64, 2, None, 7, "left_v2", "butterfly", None, False, "none"),
+    ("block_sbda_l10", 1, 200, 64, 2, None, 9, "sbda", "binary", None, False, "none"),
 ]
 
 TOPOLOGIES = ("sbda", "h8", "h8a", "h8b", "h8c", "h8d", "h8e", "binary", "h0", "h1",
@@ -218,6 +229,54 @@ def main() -> None:
                               "valid_mask": has_mask, "seam_reset": seam_reset is not None,
                               "offsets": list(topology_offsets(layer, topology=topology, total_layers=12))})
     path_arrays["manifest"] = np.frombuffer(json.dumps({"cases": path_manifest}).encode(), dtype=np.uint8)
+
+    from BiAttn.model import BiAttnBlock, BiAttnConfig  # noqa: E402  (reference code)
+
+    block_arrays: dict[str, np.ndarray] = {}
+    block_manifest = []
+    for name, batch, length, dim, heads, kv_heads, layer_index, backend, topology, ff_hidden, ff_bias, kind in \
+            BLOCK_CASES:
+        config = BiAttnConfig(vocab_size=96, dim=dim, layers=12, heads=heads, kv_heads=kv_heads,
+                              ff_hidden=ff_hidden, ff_bias=ff_bias, attention_backend=backend,
+                              path_topology=topology)
+        torch.manual_seed(2024 + layer_index * 3 + length)
+        block = BiAttnBlock(config, layer_index)
+        with torch.no_grad():
+            for norm in (block.norm1, block.norm2, block.attn.q_norm, block.attn.k_norm):
+                norm.weight.uniform_(0.5, 1.5)
+        gen = torch.Generator().manual_seed(31 + length)
+        valid_mask = seam_reset = None
+        if kind == "prefix":
+            valid_mask = torch.ones(batch, length, dtype=torch.bool)
+            valid_mask[-1, length - 7:] = False
+        elif kind == "holes_seams":
+            valid_mask = torch.rand(batch, length, generator=gen) > 0.12
+            seam_reset = torch.rand(batch, length, generator=gen) < 0.04
+        x = torch.randn(batch, length, dim, requires_grad=True)
+        y = block(x, valid_mask, seam_reset)
+        grad_y = torch.randn_like(y)
+        y.backward(grad_y)
+        record = {"x": x.detach(), "y": y.detach(), "grad_y": grad_y, "dx": x.grad}
+        if valid_mask is not None:
+            record["valid_mask"] = valid_mask.to(torch.float32)
+        if seam_reset is not None:
+            record["seam_reset"] = seam_reset.to(torch.float32)
+        for key, param in block.state_dict().items():
+            record["param." + key] = param.detach()
+        for key, param in block.named_parameters():
+            record["grad." + key] = param.grad.detach()
+        for key, value in record.items():
+            block_arrays[f"{name}/{key}"] = value.contiguous().to(torch.float32).numpy()
+        block_manifest.append({"name": name, "config": {
+            "dim": dim, "heads": heads, "kv_heads": kv_heads, "rope_theta": config.rope_theta, "layers": 12,
+            "path_sdpa": config.path_sdpa, "sbda_fused": config.sbda_fused, "sbda_backward": config.sbda_backward,
+            "attention_backend": backend, "path_topology": topology, "ff_mode": config.ff_mode,
+            "ff_mult": config.ff_mult, "ff_hidden": ff_hidden, "ff_bias": ff_bias, "dropout": config.dropout},
+            "layer_index": layer_index, "valid_mask": valid_mask is not None, "seam_reset": seam_reset is not None})
+    block_arrays["manifest"] = np.frombuffer(json.dumps({"cases": block_manifest}).encode(), dtype=np.uint8)
+    block_out = os.path.join(os.path.dirname(args.out), "block_golden.npz")
+    np.savez_compressed(block_out, **block_arrays)
+    print(f"wrote {block_out}: {len(block_manifest)} cases")
     path_out = os.path.join(os.path.dirname(args.out), "path_golden.npz")
     np.savez_compressed(path_out, **path_arrays)
     print(f"wrote {path_out}: {len(path_manifest)} cases")
