@@ -202,6 +202,36 @@ int sbda_b200_backward_masked(int dtype, sbda_shape shape, const int32_t* offset
                               sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v, void* stream);
 
 /*
+ * Attention over caller path tables (the reference's eager route for
+ * path_indices/path_valid, BiAttn/left_v2.py:212-231, 323-396; no fused
+ * counterpart there).  path_index: int32 [batch, length, n_sources] source
+ * positions (n_sources <= 4; indices outside [0, length) are not sources);
+ * source_mask: uint8 [batch, length], bit s = source s usable (the caller folds
+ * path_valid, causality, padding and segment rules in).  Vector layouts only
+ * (16-byte aligned rows, unit channel stride).
+ */
+int sbda_b200_forward_paths(int dtype, sbda_shape shape, int32_t n_sources, float scale,
+                            sbda_tensor q, sbda_tensor k, sbda_tensor v, const int32_t* path_index,
+                            const uint8_t* source_mask, sbda_tensor out, float* lse, void* stream);
+
+/* fp32 workspace floats of the path-table backward: batch * heads * length * n_sources * 2. */
+int64_t sbda_b200_paths_workspace_floats(sbda_shape shape, int32_t n_sources);
+
+/*
+ * Backward over path tables, deterministic (no atomics).  key_offsets: int32
+ * [batch, length + 1] and key_entries: int32 [batch, length * n_sources] are
+ * the inverse index per batch: entries key_offsets[b, j] .. key_offsets[b, j+1]
+ * of key_entries[b] are the codes i * n_sources + s of the (row, source)
+ * pairs that read key j, in a fixed order (the sum order).
+ */
+int sbda_b200_backward_paths(int dtype, sbda_shape shape, int32_t n_sources, float scale,
+                             sbda_tensor q, sbda_tensor k, sbda_tensor v, const int32_t* path_index,
+                             const uint8_t* source_mask, const int32_t* key_offsets,
+                             const int32_t* key_entries, sbda_tensor grad_out, const float* lse,
+                             float* workspace, int64_t workspace_floats, sbda_tensor grad_q,
+                             sbda_tensor grad_k, sbda_tensor grad_v, void* stream);
+
+/*
  * Block parts around the attention op (BiAttn/model.py:299-335).  No C
  * counterpart in the reference, which runs them as eager torch ops
  * (RMSNorm model.py:25-29, residual add model.py:325, SwiGLU gate

@@ -134,8 +134,31 @@ def source_usable(length: int, offsets: Sequence[int], valid_mask: Tensor | None
     return valid
 
 
+def path_usable(indices: Tensor, path_valid: Tensor | None, valid_mask: Tensor | None,
+                seam_reset: Tensor | None) -> Tensor:
+    """``source_valid`` ``[B, L, S]`` of the reference's eager path for a caller path
+    table (``left_v2.py:323-373``)."""
+    batch, length, source_count = indices.shape
+    valid = torch.ones(length, source_count, dtype=torch.bool)[None].expand(batch, -1, -1).clone()
+    if path_valid is not None:
+        valid &= path_valid
+    positions = torch.arange(length)
+    valid &= indices <= positions[None, :, None]
+    if valid_mask is not None:
+        valid &= valid_mask.unsqueeze(-1).expand(-1, -1, source_count).gather(1, indices)
+        if seam_reset is not None:
+            seg = seam_reset.to(torch.int64).cumsum(dim=1)
+            valid &= seg.unsqueeze(-1).expand(-1, -1, source_count).gather(1, indices) == seg[:, :, None]
+        valid[:, :, 0] |= ~valid_mask
+    elif seam_reset is not None:
+        seg = seam_reset.to(torch.int64).cumsum(dim=1)
+        valid &= seg.unsqueeze(-1).expand(-1, -1, source_count).gather(1, indices) == seg[:, :, None]
+    return valid
+
+
 def exact_attention(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int],
-                    *, use_sdpa: bool = True, usable: Tensor | None = None) -> Tensor:
+                    *, use_sdpa: bool = True, usable: Tensor | None = None,
+                    indices: Tensor | None = None) -> Tensor:
     """Exact SBDA attention on ``[B,H,L,D]`` tensors (any float dtype).
 
     Restates ``left_v2.py:335-405``: the all-valid default route, or, with
@@ -145,9 +168,14 @@ def exact_attention(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int],
     both of which the reference keeps.
     """
     batch, heads, length, head_dim = q.shape
-    indices, source_valid = path_tensors(length, offsets)
-    source_count = indices.shape[-1]
-    idx = indices[None, None, :, :, None].expand(batch, heads, length, source_count, head_dim)
+    if indices is None:  # the layer's fixed offsets
+        indices, source_valid = path_tensors(length, offsets)
+        source_count = indices.shape[-1]
+        idx = indices[None, None, :, :, None].expand(batch, heads, length, source_count, head_dim)
+    else:                # a caller path table [B, L, S]; `usable` is then required
+        source_count = indices.shape[-1]
+        idx = indices[:, None, :, :, None].expand(batch, heads, length, source_count, head_dim)
+        source_valid = None
     source_k = k.unsqueeze(3).expand(batch, heads, length, source_count, head_dim).gather(2, idx)
     source_v = v.unsqueeze(3).expand(batch, heads, length, source_count, head_dim).gather(2, idx)
     invalid = ~source_valid[None, None, :, :] if usable is None else ~usable[:, None, :, :]

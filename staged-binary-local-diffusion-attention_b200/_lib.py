@@ -98,6 +98,19 @@ def load() -> ctypes.CDLL:
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p, SbdaTensor, c_void_p,
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
+        lib.sbda_b200_forward_paths.restype = c_int
+        lib.sbda_b200_forward_paths.argtypes = [
+            c_int, SbdaShape, c_int32, c_float, SbdaTensor, SbdaTensor, SbdaTensor, c_void_p, c_void_p,
+            SbdaTensor, c_void_p, c_void_p,
+        ]
+        lib.sbda_b200_paths_workspace_floats.restype = ctypes.c_int64
+        lib.sbda_b200_paths_workspace_floats.argtypes = [SbdaShape, c_int32]
+        lib.sbda_b200_backward_paths.restype = c_int
+        lib.sbda_b200_backward_paths.argtypes = [
+            c_int, SbdaShape, c_int32, c_float, SbdaTensor, SbdaTensor, SbdaTensor, c_void_p, c_void_p,
+            c_void_p, c_void_p, SbdaTensor, c_void_p, c_void_p, ctypes.c_int64, SbdaTensor, SbdaTensor,
+            SbdaTensor, c_void_p,
+        ]
         u8p = c_void_p
         lib.sbda_b200_rms_norm_forward.restype = c_int
         lib.sbda_b200_rms_norm_forward.argtypes = [

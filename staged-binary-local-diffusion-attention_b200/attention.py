@@ -5,10 +5,11 @@ k_norm.weight``) and ``forward`` signature as the reference modules
 (``BiAttn/left_v2.py:100-198, 413-438``): ``BinaryPathAttention`` takes any
 path topology, ``SBDAttention`` is its ``topology="sbda"`` subclass.  The fused route of the reference
 (``left_v2.py:263-306``) serves the plain case; padding masks with interior
-holes and ``seam_reset`` -- which the reference sends to its eager path --
-run on the same kernels with a per-row source mask (``source_mask`` below).
-CPU tensors and caller path tables (``path_indices``/``path_valid``) raise
-instead of silently running another implementation.
+holes, ``seam_reset`` and caller path tables (``path_indices``/``path_valid``,
+up to four sources per row) -- which the reference sends to its eager path --
+run on the B200 kernels with a per-row source mask (``source_mask`` /
+``path_source_mask`` below).  CPU tensors raise instead of silently running
+another implementation.
 """
 
 from __future__ import annotations
@@ -17,7 +18,7 @@ import torch
 from torch import Tensor, nn
 
 from .norm_rope import norm_rope
-from .ops import _SBDAFunction, _check_inputs
+from .ops import _SBDAFunction, _SBDAPathFunction, _check_inputs
 from .topology import PATH_TOPOLOGIES, topology_offsets
 
 
@@ -107,15 +108,34 @@ class BinaryPathAttention(nn.Module):
             raise ValueError("valid_mask must be bool with input shape")
         if seam_reset is not None and (seam_reset.shape != (batch, length) or seam_reset.dtype != torch.bool):
             raise ValueError("seam_reset must be bool with input shape")
-        if path_indices is not None or path_valid is not None:
-            raise NotImplementedError("caller path tables are not served by the B200 SBDA kernels")
+        if path_indices is not None:  # the reference's checks, left_v2.py:212-231
+            if path_indices.ndim != 3 or path_indices.shape[:2] != (batch, length):
+                raise ValueError("path_indices must have shape [batch, sequence, source_count]")
+            if path_indices.dtype != torch.long:
+                raise ValueError("path_indices must use torch.long")
+            if path_indices.device != x.device:
+                raise ValueError("path_indices must be on the same device as x")
+            if path_valid is None:
+                path_valid = torch.ones_like(path_indices, dtype=torch.bool)
+            elif (path_valid.shape != path_indices.shape or path_valid.dtype != torch.bool
+                  or path_valid.device != x.device):
+                raise ValueError("path_valid must match path_indices as a bool tensor")
+            if path_indices.numel() and (int(path_indices.min()) < 0 or int(path_indices.max()) >= length):
+                raise ValueError("path_indices contains an out-of-range source")
+            if not 1 <= path_indices.shape[-1] <= 4:
+                raise ValueError("the B200 path-table kernels take one to four sources per row")
+        elif path_valid is not None:
+            raise ValueError("path_valid needs path_indices")
         if not x.is_cuda:
             raise RuntimeError("the B200 SBDA module requires CUDA inputs")
-        # A prefix mask (left_v2.py:258-262) never hides a source from a valid row
-        # (sources are earlier positions), so it only needs the output multiply.
-        holes = (valid_mask is not None and valid_mask.shape[1] >= 2
-                 and not bool(torch.all(~valid_mask[:, 1:] | valid_mask[:, :-1])))
-        mask = self.source_mask(valid_mask, seam_reset) if holes or seam_reset is not None else None
+        if path_indices is not None:
+            mask = self.path_source_mask(path_indices, path_valid, valid_mask, seam_reset)
+        else:
+            # A prefix mask (left_v2.py:258-262) never hides a source from a valid row
+            # (sources are earlier positions), so it only needs the output multiply.
+            holes = (valid_mask is not None and valid_mask.shape[1] >= 2
+                     and not bool(torch.all(~valid_mask[:, 1:] | valid_mask[:, :-1])))
+            mask = self.source_mask(valid_mask, seam_reset) if holes or seam_reset is not None else None
         q = self.q(x).view(batch, length, self.heads, self.head_dim)
         k = self.k(x).view(batch, length, self.kv_heads, self.head_dim)
         v = self.v(x).view(batch, length, self.kv_heads, self.head_dim)
@@ -125,10 +145,34 @@ class BinaryPathAttention(nn.Module):
         q = q.permute(0, 2, 1, 3)
         k = k.permute(0, 2, 1, 3)
         v = v.permute(0, 2, 1, 3)
-        _check_inputs(q, k, v, self.offsets, gqa=self.kv_heads != self.heads, source_counts=(1, 2, 3, 4))
-        attended = _SBDAFunction.apply(q, k, v, self.offsets, mask)
+        if path_indices is not None:
+            _check_inputs(q, k, v, (0,), gqa=self.kv_heads != self.heads, source_counts=(1,))
+            attended = _SBDAPathFunction.apply(q, k, v, path_indices.to(torch.int32).contiguous(), mask)
+        else:
+            _check_inputs(q, k, v, self.offsets, gqa=self.kv_heads != self.heads, source_counts=(1, 2, 3, 4))
+            attended = _SBDAFunction.apply(q, k, v, self.offsets, mask)
         attended = attended.transpose(1, 2).reshape(batch, length, dim)
         return self.out(attended)
+
+    def path_source_mask(self, path_indices: Tensor, path_valid: Tensor, valid_mask: Tensor | None,
+                         seam_reset: Tensor | None) -> Tensor:
+        """Source bits (uint8 ``[B, L]``) of a caller path table, ``left_v2.py:340-373``: a
+        source is usable if ``path_valid`` says so, it is not after the row, and (with the
+        masks) it is not padding and lies in the row's segment; padded rows keep source 0."""
+        batch, length, sources = path_indices.shape
+        positions = torch.arange(length, device=path_indices.device)
+        usable = path_valid & (path_indices <= positions[None, :, None])
+        if valid_mask is not None:
+            usable = usable & torch.gather(valid_mask, 1, path_indices.reshape(batch, -1)).view_as(usable)
+        if seam_reset is not None:
+            segment = seam_reset.to(torch.int64).cumsum(dim=1)
+            source_segment = torch.gather(segment, 1, path_indices.reshape(batch, -1)).view_as(usable)
+            usable = usable & (source_segment == segment[:, :, None])
+        if valid_mask is not None:
+            usable = usable.clone()
+            usable[:, :, 0] |= ~valid_mask
+        weights = (1 << torch.arange(sources, device=path_indices.device)).to(torch.uint8)
+        return (usable.to(torch.uint8) * weights).sum(dim=-1).to(torch.uint8).contiguous()
 
     def source_mask(self, valid_mask: Tensor | None, seam_reset: Tensor | None) -> Tensor:
         """Per-row source bits (uint8 ``[B, L]``, bit s = source s usable), ``left_v2.py:349-373``.

@@ -200,6 +200,69 @@ class _SBDAFunction(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+def path_key_index(index: Tensor, source_mask: Tensor) -> tuple[Tensor, Tensor]:
+    """Inverse of a path table: per batch, for each key position j, the codes
+    ``i * S + s`` of the (row, source) pairs whose source is j and usable, sorted by
+    (j, code) so the backward sums them in a fixed order.  Returns int32
+    ``(offsets [B, L + 1], entries [B, L * S])``; unused entry slots are -1."""
+    batch, length, sources = index.shape
+    usable = ((source_mask.to(torch.int32)[:, :, None] >> torch.arange(sources, device=index.device)) & 1).bool()
+    usable &= (index >= 0) & (index < length)
+    codes = torch.arange(length * sources, device=index.device, dtype=torch.int64).expand(batch, -1)
+    keys = torch.where(usable.reshape(batch, -1), index.reshape(batch, -1).to(torch.int64),
+                       torch.full_like(codes, length))          # unused pairs sort last
+    order = torch.argsort(keys * (length * sources) + codes, dim=1)
+    entries = torch.where(torch.gather(keys, 1, order) < length, order, torch.full_like(order, -1))
+    counts = torch.zeros(batch, length + 1, device=index.device, dtype=torch.int64)
+    counts.scatter_add_(1, keys, torch.ones_like(keys))
+    offsets = torch.zeros(batch, length + 1, device=index.device, dtype=torch.int64)
+    offsets[:, 1:] = torch.cumsum(counts[:, :length], dim=1)
+    return offsets.to(torch.int32).contiguous(), entries.to(torch.int32).contiguous()
+
+
+class _SBDAPathFunction(torch.autograd.Function):
+    """Attention over a caller path table (``left_v2.py:323-396``): ``index`` int32
+    ``[B, L, S]``, ``source_mask`` uint8 ``[B, L]`` (bit s = source s usable)."""
+
+    @staticmethod
+    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, index: Tensor, source_mask: Tensor) -> Tensor:
+        batch, heads, length, head_dim = q.shape
+        sources = index.shape[-1]
+        out = torch.empty_like(q)
+        lse = torch.empty((batch, heads, length), device=q.device, dtype=torch.float32)
+        lib = _lib.load()
+        with torch.cuda.device(q.device):
+            status = lib.sbda_b200_forward_paths(
+                _DTYPES[q.dtype], _shape(q, k), sources, head_dim ** -0.5, _tensor_arg(q), _tensor_arg(k),
+                _tensor_arg(v), index.data_ptr(), source_mask.data_ptr(), _tensor_arg(out), lse.data_ptr(),
+                torch.cuda.current_stream(q.device).cuda_stream)
+        _lib.raise_for_status(status, "sbda_b200_forward_paths")
+        ctx.save_for_backward(q, k, v, index, source_mask, lse)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out: Tensor):
+        q, k, v, index, source_mask, lse = ctx.saved_tensors
+        sources = index.shape[-1]
+        grad_out = grad_out.to(q.dtype).contiguous()
+        if grad_out.data_ptr() % 16:
+            grad_out = grad_out.clone()
+        offsets, entries = path_key_index(index, source_mask)
+        lib = _lib.load()
+        shape = _shape(q, k)
+        workspace = torch.empty(lib.sbda_b200_paths_workspace_floats(shape, sources), device=q.device,
+                                dtype=torch.float32)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        with torch.cuda.device(q.device):
+            status = lib.sbda_b200_backward_paths(
+                _DTYPES[q.dtype], shape, sources, q.shape[-1] ** -0.5, _tensor_arg(q), _tensor_arg(k),
+                _tensor_arg(v), index.data_ptr(), source_mask.data_ptr(), offsets.data_ptr(), entries.data_ptr(),
+                _tensor_arg(grad_out), lse.data_ptr(), workspace.data_ptr(), workspace.numel(), _tensor_arg(dq),
+                _tensor_arg(dk), _tensor_arg(dv), torch.cuda.current_stream(q.device).cuda_stream)
+        _lib.raise_for_status(status, "sbda_b200_backward_paths")
+        return dq, dk, dv, None, None
+
+
 def _apply(q: Tensor, k: Tensor, v: Tensor, offsets: Tensor | Sequence[int], *, gqa: bool) -> Tensor:
     values = host_offsets(offsets)
     _check_inputs(q, k, v, values, gqa=gqa)

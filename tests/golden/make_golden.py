@@ -88,6 +88,17 @@ BLOCK_CASES = [
     ("block_sbda_l10", 1, 200, 64, 2, None, 9, "sbda", "binary", None, False, "none"),
 ]
 
+# Modules given caller path tables (left_v2.py:212-231, 323-373), on the
+# reference's eager path: (name, batch, length, dim, heads, kv_heads, sources,
+# path_valid drop rate, padding holes, segment resets).  Tables are causal random
+# jumps (plus the row itself as source 0).
+TABLE_CASES = [
+    ("table_s3", 2, 120, 32, 2, 2, 3, 0.0, False, False),
+    ("table_s4_valid", 1, 200, 32, 2, 2, 4, 0.2, False, False),
+    ("table_s2_holes_seams", 2, 90, 32, 2, 2, 2, 0.1, True, True),
+    ("table_s3_gqa", 1, 150, 64, 4, 2, 3, 0.0, True, False),
+]
+
 TOPOLOGIES = ("sbda", "h8", "h8a", "h8b", "h8c", "h8d", "h8e", "binary", "h0", "h1",
               "h7", "local_jump", "longformer_local")
 
@@ -228,6 +239,42 @@ def main() -> None:
                               "kv_heads": kv_heads, "layer": layer, "topology": topology,
                               "valid_mask": has_mask, "seam_reset": seam_reset is not None,
                               "offsets": list(topology_offsets(layer, topology=topology, total_layers=12))})
+    for name, batch, length, dim, heads, kv_heads, sources, drop, holes, seams in TABLE_CASES:
+        gen = torch.Generator().manual_seed(555 + length + sources)
+        positions = torch.arange(length)
+        jumps = torch.randint(0, 64, (batch, length, sources), generator=gen)
+        jumps[:, :, 0] = 0
+        indices = (positions[None, :, None] - jumps).clamp_min(0)
+        path_valid = torch.rand(batch, length, sources, generator=gen) >= drop
+        valid_mask = (torch.rand(batch, length, generator=gen) > 0.1) if holes else None
+        seam_reset = (torch.rand(batch, length, generator=gen) < 0.05) if seams else None
+        torch.manual_seed(4242 + length)
+        attn = left_v2.BinaryPathAttention(dim, heads, 1, kv_heads=kv_heads, topology="h4_greedy",
+                                           total_layers=12, use_fused=False)
+        with torch.no_grad():
+            attn.q_norm.weight.uniform_(0.5, 1.5)
+            attn.k_norm.weight.uniform_(0.5, 1.5)
+        x = torch.randn(batch, length, dim, requires_grad=True)
+        y = attn(x, valid_mask=valid_mask, seam_reset=seam_reset, path_indices=indices, path_valid=path_valid)
+        grad_y = torch.randn_like(y)
+        y.backward(grad_y)
+        record = {"x": x.detach(), "y": y.detach(), "grad_y": grad_y, "dx": x.grad,
+                  "path_indices": indices.to(torch.float32), "path_valid": path_valid.to(torch.float32)}
+        if valid_mask is not None:
+            record["valid_mask"] = valid_mask.to(torch.float32)
+        if seam_reset is not None:
+            record["seam_reset"] = seam_reset.to(torch.float32)
+        for key, param in attn.state_dict().items():
+            record["param." + key] = param.detach()
+        for key, param in attn.named_parameters():
+            record["grad." + key] = param.grad.detach()
+        for key, value in record.items():
+            path_arrays[f"{name}/{key}"] = value.contiguous().to(torch.float32).numpy()
+        path_manifest.append({"name": name, "batch": batch, "length": length, "dim": dim, "heads": heads,
+                              "kv_heads": kv_heads, "layer": 1, "topology": "h4_greedy",
+                              "valid_mask": valid_mask is not None, "seam_reset": seam_reset is not None,
+                              "path_table": True,
+                              "offsets": list(topology_offsets(1, topology="h4_greedy", total_layers=12))})
     path_arrays["manifest"] = np.frombuffer(json.dumps({"cases": path_manifest}).encode(), dtype=np.uint8)
 
     from BiAttn.model import BiAttnBlock, BiAttnConfig  # noqa: E402  (reference code)

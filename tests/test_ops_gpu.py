@@ -311,8 +311,9 @@ def test_several_far_offsets(length):
 
 def test_path_topology_modules_match_reference_golden(path_golden):
     """BinaryPathAttention over other topologies (butterfly, radix4, mesh, h2, h8a, binary, the
-    three-source h5 layer, GQA), and modules with padding holes and segment resets (the
-    reference's eager route), reproduce the reference module: output, dx and parameter grads."""
+    three-source h5 layer, GQA), modules with padding holes and segment resets, and modules given
+    caller path tables (the reference's eager routes) reproduce the reference module: output, dx
+    and parameter grads."""
     for case in path_golden.cases:
         name = case["name"]
         module = sbda_b200.BinaryPathAttention(case["dim"], case["heads"], case["layer"],
@@ -326,7 +327,11 @@ def test_path_topology_modules_match_reference_golden(path_golden):
         x = path_golden.get(name, "x").cuda().requires_grad_()
         valid_mask = path_golden.get(name, "valid_mask").cuda().bool() if case.get("valid_mask") else None
         seam_reset = path_golden.get(name, "seam_reset").cuda().bool() if case.get("seam_reset") else None
-        y = module(x, valid_mask=valid_mask, seam_reset=seam_reset)
+        tables = {}
+        if case.get("path_table"):
+            tables = dict(path_indices=path_golden.get(name, "path_indices").cuda().long(),
+                          path_valid=path_golden.get(name, "path_valid").cuda().bool())
+        y = module(x, valid_mask=valid_mask, seam_reset=seam_reset, **tables)
         y.backward(path_golden.get(name, "grad_y").cuda())
         tol = dict(rtol=2e-5, atol=2e-5)
         torch.testing.assert_close(y.detach().cpu(), path_golden.get(name, "y"), **tol, msg=name)
@@ -370,3 +375,39 @@ def test_source_masks_match_oracle(dtype):
             _close(kk.grad, rdk, dtype, "dK " + tag, rtol=2.0 ** -8 if dtype != torch.float32 else None)
             _close(vv.grad, rdv, dtype, "dV " + tag, rtol=2.0 ** -8 if dtype != torch.float32 else None)
             assert bool(rows.any())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_path_tables_match_oracle(dtype):
+    """Caller path tables through sbda_b200_{forward,backward}_paths against the oracle's
+    gather route (left_v2.py:323-396): random causal tables, path_valid, holes, seams, GQA."""
+    g = torch.Generator().manual_seed(8)
+    for length, sources, kv_heads in ((257, 3, 4), (1000, 4, 2), (64, 1, 4), (3000, 2, 1)):
+        q, k, v, do = _inputs(2, 4, length, 64, dtype, kv_heads=kv_heads, seed=length)
+        positions = torch.arange(length)
+        jumps = torch.randint(0, 400, (2, length, sources), generator=g)
+        indices = (positions[None, :, None] - jumps).clamp_min(0)
+        indices[0, 5:, -1] = torch.randint(0, length, (length - 5,), generator=g)  # some future sources
+        path_valid = torch.rand(2, length, sources, generator=g) > 0.15
+        valid_mask = torch.rand(2, length, generator=g) > 0.1
+        seam_reset = torch.rand(2, length, generator=g) < 0.02
+        module = sbda_b200.BinaryPathAttention(32, 2, 1, topology="h4_greedy")
+        bits = module.path_source_mask(indices.cuda(), path_valid.cuda(), valid_mask.cuda(), seam_reset.cuda())
+        qq, kk, vv = (t.detach().requires_grad_() for t in (q, k, v))
+        out = sbda_b200.ops._SBDAPathFunction.apply(qq, kk, vv, indices.cuda().to(torch.int32).contiguous(), bits)
+        out.backward(do)
+        usable = orc.path_usable(indices, path_valid, valid_mask, seam_reset)
+        group = 4 // kv_heads
+        qc, kc, vc, doc = (t.detach().cpu().double() for t in (q, k, v, do))
+        kc, vc = kc.repeat_interleave(group, 1), vc.repeat_interleave(group, 1)
+        qc, kc, vc = (t.requires_grad_() for t in (qc, kc, vc))
+        ref = orc.exact_attention(qc, kc, vc, (), usable=usable, indices=indices)
+        ref.backward(doc)
+        rdk = kc.grad.view(2, kv_heads, group, length, 64).sum(2)
+        rdv = vc.grad.view(2, kv_heads, group, length, 64).sum(2)
+        tag = f"L {length} S {sources} kv {kv_heads} {dtype}"
+        grad_rtol = 2.0 ** -8 if dtype != torch.float32 else None
+        _close(out, ref.detach(), dtype, "O " + tag)
+        _close(qq.grad, qc.grad, dtype, "dQ " + tag)
+        _close(kk.grad, rdk, dtype, "dK " + tag, rtol=grad_rtol)
+        _close(vv.grad, rdv, dtype, "dV " + tag, rtol=grad_rtol)
