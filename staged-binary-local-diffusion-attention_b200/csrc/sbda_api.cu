@@ -223,6 +223,10 @@ int make_plan(const int32_t* off, int n, int64_t L, int64_t D, int e, Plan* pl) 
 // Plan of the windowed kernels (sbda_v2.cu).  They serve MHA schedules whose
 // near offsets lie in {0, 1, 2} with at most one far offset d > 2; the
 // backward walks chains when d is a multiple of the tile height.
+// K/V rows the forward stages before its tile: the far offset when it is shorter
+// than a tile (its sources then share the window), else the 2 rows of offsets 1, 2.
+int fwd_window_lead(const V2Geometry& g, int T) { return g.has_far && g.d < T ? g.d : 2; }
+
 // LSE rows staged per backward step: the Q/dO slot height rounded up to 32
 // (fp32 rows; 128-byte multiples).
 int lse_box_rows(const V2Geometry& g, int T) { return (T + g.halo + 31) / 32 * 32; }
@@ -269,8 +273,11 @@ int balanced_segment(int64_t chains, int len, bool pre, int64_t slots) {
   return best;
 }
 
+// L: rows of this call (a shard when sequence-sharded); total_L: positions of
+// the whole sequence (offsets at or beyond it never have a source).
 bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, int64_t B, int64_t H,
-             V2Plan* pl) {
+             V2Plan* pl, int64_t total_L = -1) {
+  if (total_L < 0) total_L = L;
   if (G != 1) return false;
   const int pitch = row_pitch(D, e);
   const int lane_bytes = e == 4 ? 32 : 16;
@@ -284,17 +291,20 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
     if (off[s] == 0) g.has0 = 1;
     else if (off[s] == 1) g.has1 = 1;
     else if (off[s] == 2) g.has2 = 1;
-    else if (off[s] < L) {
+    else if (off[s] < total_L) {
       g.d = off[s];
       ++nfar;
     }
-    // a far offset >= L never has a valid source: it drops out of every row
+    // a far offset >= total_L never has a valid source: it drops out of every row
   }
   if (nfar > 1) return false;
   g.has_far = nfar;
   g.nT = (int)((L + T - 1) / T);
-  if (g.has_far && g.d % T == 0 && g.d / T < g.nT) {
+  if (g.has_far && g.d % T == 0) {
+    // Chains t, t + R, ... of this call's tiles; a shard shorter than d holds
+    // one tile of each of its nT chains.
     g.R = g.d / T;
+    g.chains = g.R < g.nT ? g.R : g.nT;
     g.A = (g.nT + g.R - 1) / g.R;
     g.rem = g.nT - (g.A - 1) * g.R;
   }
@@ -316,13 +326,16 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   pl->lpr = lpr;
   pl->tile = T;
   pl->pitch = pitch;
-  pl->smem_fwd = (size_t)(T + 2 * (T + 2) + 2 * T * g.has_far) * pitch + 16;
+  // Forward: [Q] + K/V rows [i0 - lead, i0 + T) (lead = d for a far offset under a
+  // tile, else 2) + a separate far tile for longer far offsets.
+  const int fwd_lead = fwd_window_lead(g, T);
+  pl->smem_fwd = (size_t)(T + 2 * (T + fwd_lead) + (g.has_far && g.d >= T ? 2 * T : 0)) * pitch + 16;
   pl->lse_box = lse_box_rows(g, T);
   pl->smem_bwd = bwd_smem(g, T, pitch);
   if (pl->smem_fwd > kMaxSmem || pl->smem_bwd > kMaxSmem) return false;
   // Backward work split: walks of `chains` x `len` tiles cut into segments,
   // one CTA each.
-  const int64_t chains = g.mode == 0 ? B * H * (int64_t)g.R : B * H;
+  const int64_t chains = g.mode == 0 ? B * H * (int64_t)g.chains : B * H;
   const int len = g.mode == 0 ? g.A : g.nT;
   g.seg = balanced_segment(chains, len, g.mode != 1, (int64_t)sm_count() * 3);
   g.segs = (len + g.seg - 1) / g.seg;
@@ -518,6 +531,7 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
     p.out = arg_of(out);
     p.lse = lse;
     p.status = status_ptr();
+    p.sh = single_shard(L, lse);
     FwdMaps maps;
     memset(&maps, 0, sizeof(maps));
     bool tma = vec;
@@ -526,8 +540,8 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
       tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p2.pitch, p2.tile) &&
             encode_map(&maps.kT, &p.slots_k, k, dtype, B, H, L, D, p2.pitch, p2.tile) &&
             encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
-            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, 2) &&
-            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, 2);
+            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, fwd_window_lead(p2.g, p2.tile)) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, fwd_window_lead(p2.g, p2.tile));
     }
     return v2_forward(dtype, tma, maps, p, p2, s);
   }
@@ -604,6 +618,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
     p.dv = arg_of(grad_v);
     p.lse = lse;
     p.status = status_ptr();
+    p.sh = single_shard(L, lse);
     BwdMaps maps;
     memset(&maps, 0, sizeof(maps));
     bool tma = vec;
@@ -776,7 +791,39 @@ extern "C" int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int3
   if (!q.data || !out.data || !lse) return SBDA_ERR_INVALID;
   for (int r = 0; r < world; ++r)
     if (!k_ranks[r].data || !v_ranks[r].data) return SBDA_ERR_INVALID;
+  // One shard is the whole sequence: the unsharded kernels (windowed where they apply).
+  if (world == 1) return sbda_b200_forward(dtype, shape, offsets, n_offsets, scale, q, k_ranks[0], v_ranks[0], out, lse, stream);
   const int e = elem_size(dtype);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  {  // The windowed kernels, when they serve the schedule and every view suits the copy engine.
+    V2Plan p2;
+    if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, Ls, D, e, H / Hkv, B, H, &p2, world * Ls) &&
+        Ls % p2.tile == 0 && vector_ok(q, B, H, Ls, D, e) && vector_ok(out, B, H, Ls, D, e)) {
+      FwdV2Params p;
+      memset(&p, 0, sizeof(p));
+      p.B = (int)B;
+      p.H = (int)H;
+      p.L = (int)Ls;
+      p.D = (int)D;
+      p.scale = scale;
+      p.g = p2.g;
+      p.q = arg_of(q);
+      p.k = arg_of(k_ranks[rank]);
+      p.v = arg_of(v_ranks[rank]);
+      p.out = arg_of(out);
+      p.lse = lse;
+      p.status = status_ptr();
+      p.sh = shard_info(rank, world, Ls);
+      p.sh.lse[rank] = lse;
+      ShardFwdMaps maps;
+      memset(&maps, 0, sizeof(maps));
+      if (encode_ranks(maps.kT, &p.slots_k, k_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
+          encode_ranks(maps.vT, &p.slots_v, v_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
+          encode_ranks(maps.kH, nullptr, k_ranks, world, dtype, B, H, Ls, D, p2.pitch, fwd_window_lead(p2.g, p2.tile)) &&
+          encode_ranks(maps.vH, nullptr, v_ranks, world, dtype, B, H, Ls, D, p2.pitch, fwd_window_lead(p2.g, p2.tile)))
+        return v2_forward_sharded(dtype, maps, p, p2, s);
+    }
+  }
   Plan pl;
   st = plan_sharded(offsets, n_offsets, Ls, D, e, world, &pl);
   if (st != SBDA_OK) return st;
@@ -830,7 +877,51 @@ extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int
   for (int r = 0; r < world; ++r)
     if (!q_ranks[r].data || !k_ranks[r].data || !v_ranks[r].data || !grad_out_ranks[r].data || !lse_ranks[r])
       return SBDA_ERR_INVALID;
+  if (world == 1)
+    return sbda_b200_backward(dtype, shape, offsets, n_offsets, scale, q_ranks[0], k_ranks[0], v_ranks[0],
+                              grad_out_ranks[0], lse_ranks[0], grad_q, grad_k, grad_v, stream);
   const int e = elem_size(dtype);
+  {  // The windowed kernels, when they serve the schedule and every view suits the copy engine.
+    V2Plan p2;
+    if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, Ls, D, e, H / Hkv, B, H, &p2, world * Ls) &&
+        Ls % p2.tile == 0 && vector_ok(grad_q, B, H, Ls, D, e) && vector_ok(grad_k, B, H, Ls, D, e) &&
+        vector_ok(grad_v, B, H, Ls, D, e)) {
+      BwdV2Params p;
+      memset(&p, 0, sizeof(p));
+      p.B = (int)B;
+      p.H = (int)H;
+      p.L = (int)Ls;
+      p.D = (int)D;
+      p.scale = scale;
+      p.g = p2.g;
+      p.q = arg_of(q_ranks[rank]);
+      p.k = arg_of(k_ranks[rank]);
+      p.v = arg_of(v_ranks[rank]);
+      p.dout = arg_of(grad_out_ranks[rank]);
+      p.dq = arg_of(grad_q);
+      p.dk = arg_of(grad_k);
+      p.dv = arg_of(grad_v);
+      p.lse = lse_ranks[rank];
+      p.status = status_ptr();
+      p.lse_tma = 0;  // LSE rows past the shard end are the next rank's: read per row
+      p.lse_box = p2.lse_box;
+      p.sh = shard_info(rank, world, Ls);
+      for (int r = 0; r < world; ++r) p.sh.lse[r] = lse_ranks[r];
+      const int hz = p2.g.halo;
+      const int lead = p2.g.mode == 2 ? p2.g.d : hz;
+      ShardBwdMaps maps;
+      memset(&maps, 0, sizeof(maps));
+      if (encode_ranks(maps.qT, &p.slots_q, q_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
+          encode_ranks(maps.dT, &p.slots_d, grad_out_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
+          encode_ranks(maps.kT, &p.slots_k, k_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
+          encode_ranks(maps.vT, &p.slots_v, v_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
+          encode_ranks(maps.qH, nullptr, q_ranks, world, dtype, B, H, Ls, D, p2.pitch, hz) &&
+          encode_ranks(maps.dH, nullptr, grad_out_ranks, world, dtype, B, H, Ls, D, p2.pitch, hz) &&
+          encode_ranks(maps.kH, nullptr, k_ranks, world, dtype, B, H, Ls, D, p2.pitch, lead) &&
+          encode_ranks(maps.vH, nullptr, v_ranks, world, dtype, B, H, Ls, D, p2.pitch, lead))
+        return v2_backward_sharded(dtype, maps, p, p2, reinterpret_cast<cudaStream_t>(stream));
+    }
+  }
   Plan pl;
   st = plan_sharded(offsets, n_offsets, Ls, D, e, world, &pl);
   if (st != SBDA_OK) return st;

@@ -90,6 +90,7 @@ struct ShardFwdMaps {
 struct ShardBwdMaps {
   CUtensorMap qT[kMaxShards], qH[kMaxShards], dT[kMaxShards], dH[kMaxShards];
   CUtensorMap kT[kMaxShards], kH[kMaxShards], vT[kMaxShards], vH[kMaxShards];
+  CUtensorMap lseT;  // unused: sharded calls read LSE rows through ShardInfo::lse
 };
 
 // Map and map coordinate of the rows starting at global position gpos.
@@ -577,20 +578,22 @@ struct V2Geometry {
   int halo;              // backward: consumer halo rows past the tile (2, or d in mode 1)
   int seg;               // backward: tiles per CTA
   int segs;              // backward: segments per chain (mode 0) or per (b, h) (mode 1)
+  int chains;            // backward chain walks per (b, h): min(R, nT)
 };
 
 struct FwdV2Params {
-  int B, H, L, D;
+  int B, H, L, D;        // L: positions of this call's rows (the shard when sharded)
   float scale;
   V2Geometry g;
   TensorArg q, k, v, out;
   float* lse;
   unsigned slots_q, slots_k, slots_v;
   unsigned* status;
+  ShardInfo sh;          // one shard (pos0 = 0, total_len = L) unless sequence-sharded
 };
 
 struct BwdV2Params {
-  int B, H, L, D;
+  int B, H, L, D;        // L: positions of this call's rows (the shard when sharded)
   float scale;
   V2Geometry g;
   TensorArg q, k, v, dout, dq, dk, dv;
@@ -599,6 +602,7 @@ struct BwdV2Params {
   unsigned* status;
   int lse_tma;   // 1: LSE rows staged by the copy engine with Q/dO (L % 4 == 0)
   int lse_box;   // rows of that box (Q/dO slot height rounded up to 32)
+  ShardInfo sh;  // one shard (pos0 = 0, total_len = L) unless sequence-sharded
 };
 
 // Uniform kernels (sbda_v3.cu): every source a shifted tile.
@@ -654,6 +658,10 @@ struct V2Plan {
 };
 
 int v2_forward(int dtype, bool tma, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st);
+int v2_forward_sharded(int dtype, const ShardFwdMaps& maps, const FwdV2Params& p, const V2Plan& pl,
+                       cudaStream_t st);
+int v2_backward_sharded(int dtype, const ShardBwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
+                        cudaStream_t st);
 int v3_forward(int dtype, bool tma, const FwdMaps& maps, const V3Params& p, const V3Plan& pl, cudaStream_t st);
 int v3_backward(int dtype, bool tma, const BwdMaps& maps, const V3Params& p, const V3Plan& pl, cudaStream_t st);
 int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,

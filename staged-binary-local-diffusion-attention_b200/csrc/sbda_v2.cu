@@ -63,8 +63,8 @@ __device__ __forceinline__ int chain_tile_v2(int idx, int R, int A, int rem) {
 
 // Source-set shapes of the forward: 0 = flags read at run time, 1 = {0, 1},
 // 2 = {0, 2}, 3 = {0, 1, 2, d}.
-template <typename TE, int LPR, bool TMA, int SHAPE>
-__global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_constant__ FwdMaps maps,
+template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = FwdMaps>
+__global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_constant__ Maps maps,
                                                                const FwdV2Params p) {
   constexpr int T = v2_tile(LPR);
   constexpr int P = LPR * FragIO<TE>::kLaneBytes;
@@ -86,12 +86,18 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
 
   // The copy-engine path reads each group's Q rows straight into registers
   // (no Q tile in shared memory: more CTAs per SM); the generic path stages Q.
+  // K/V rows [i0 - lead, i0 + T): lead = 2 (offsets 1, 2), or d when the far
+  // offset is shorter than a tile -- its sources then lie in the same window
+  // (staged once, as a d-row box and the tile, both tile-aligned).  A far offset
+  // of a tile or more gets its own tile [i0 - d, i0 - d + T).
+  const bool near_far = far && g.d < T;
+  const int lead = near_far ? g.d : 2;
   uint8_t* Qs = smem;
-  uint8_t* Kn = smem + (TMA ? 0 : T * P);  // positions [i0-2, i0+T)
-  uint8_t* Vn = Kn + (T + 2) * P;
-  uint8_t* Kf = Vn + (T + 2) * P;  // positions [i0-d, i0-d+T)
-  uint8_t* Vf = Kf + (far ? T * P : 0);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(Vf + (far ? T * P : 0));
+  uint8_t* Kn = smem + (TMA ? 0 : T * P);
+  uint8_t* Vn = Kn + (T + lead) * P;
+  uint8_t* Kf = near_far ? Kn : Vn + (T + lead) * P;  // row r = source of query r
+  uint8_t* Vf = near_far ? Vn : Kf + T * P;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(Vn + (T + lead) * P + (far && !near_far ? 2 * T * P : 0));
 
   const int a = grp * 4;
   RowWords<TE> qw[4];
@@ -102,14 +108,17 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
     }
     __syncthreads();
     if (tid == 0) {
-      mbar_arrive_expect_tx(bar, (uint32_t)((T * (2 + 2 * far) + 4) * P));
-      tma_rows(Kn, &maps.kH, bar, p.slots_k, i0 - 2, h, b);
-      tma_rows(Vn, &maps.vH, bar, p.slots_v, i0 - 2, h, b);
-      tma_rows(Kn + 2 * P, &maps.kT, bar, p.slots_k, i0, h, b);
-      tma_rows(Vn + 2 * P, &maps.vT, bar, p.slots_v, i0, h, b);
-      if (far) {
-        tma_rows(Kf, &maps.kT, bar, p.slots_k, i0 - g.d, h, b);
-        tma_rows(Vf, &maps.vT, bar, p.slots_v, i0 - g.d, h, b);
+      // Each box lies in one rank's shard; pick_map gives its map and local row.
+      const int ig = p.sh.pos0 + i0;
+      int c;
+      mbar_arrive_expect_tx(bar, (uint32_t)((2 * (T + lead) + (far && !near_far ? 2 * T : 0)) * P));
+      tma_rows(Kn, pick_map(maps.kH, p.sh, ig - lead, c), bar, p.slots_k, c, h, b);
+      tma_rows(Vn, pick_map(maps.vH, p.sh, ig - lead, c), bar, p.slots_v, c, h, b);
+      tma_rows(Kn + lead * P, pick_map(maps.kT, p.sh, ig, c), bar, p.slots_k, c, h, b);
+      tma_rows(Vn + lead * P, pick_map(maps.vT, p.sh, ig, c), bar, p.slots_v, c, h, b);
+      if (far && !near_far) {
+        tma_rows(Kf, pick_map(maps.kT, p.sh, ig - g.d, c), bar, p.slots_k, c, h, b);
+        tma_rows(Vf, pick_map(maps.vT, p.sh, ig - g.d, c), bar, p.slots_v, c, h, b);
       }
     }
     // Q rows of this group, in flight while the K/V copies land.
@@ -127,9 +136,9 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   } else {
     constexpr int PE = P / sizeof(TE);
     generic_rows<TE>(Qs, p.q, b, h, i0, T, p.L, p.D, PE);
-    generic_rows<TE>(Kn, p.k, b, h, i0 - 2, T + 2, p.L, p.D, PE);
-    generic_rows<TE>(Vn, p.v, b, h, i0 - 2, T + 2, p.L, p.D, PE);
-    if (far) {
+    generic_rows<TE>(Kn, p.k, b, h, i0 - lead, T + lead, p.L, p.D, PE);
+    generic_rows<TE>(Vn, p.v, b, h, i0 - lead, T + lead, p.L, p.D, PE);
+    if (far && !near_far) {
       generic_rows<TE>(Kf, p.k, b, h, i0 - g.d, T, p.L, p.D, PE);
       generic_rows<TE>(Vf, p.v, b, h, i0 - g.d, T, p.L, p.D, PE);
     }
@@ -144,14 +153,15 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   const int src_k = (l >> 1) & 3;
   const bool src_has = src_k == 0 ? has0 : (src_k == 1 ? has1 : (src_k == 2 ? has2 : far));
   const int src_off = src_k == 0 ? 0 : (src_k == 1 ? 1 : (src_k == 2 ? 2 : g.d));
-  Frag k1 = FragIO<TE>::load(Kn + (a + 1) * P, l), k2 = FragIO<TE>::load(Kn + a * P, l);
-  Frag v1 = FragIO<TE>::load(Vn + (a + 1) * P, l), v2 = FragIO<TE>::load(Vn + a * P, l);
+  Frag k1 = FragIO<TE>::load(Kn + (a + lead - 1) * P, l), k2 = FragIO<TE>::load(Kn + (a + lead - 2) * P, l);
+  Frag v1 = FragIO<TE>::load(Vn + (a + lead - 1) * P, l), v2 = FragIO<TE>::load(Vn + (a + lead - 2) * P, l);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = a + i, pos = i0 + r;
+    const int pg = p.sh.pos0 + pos;  // global position: source masks
     const Frag q = TMA ? FragIO<TE>::from_words(qw[i].w) : FragIO<TE>::load(Qs + r * P, l);
-    const Frag k0 = FragIO<TE>::load(Kn + (r + 2) * P, l);
-    const Frag v0 = FragIO<TE>::load(Vn + (r + 2) * P, l);
+    const Frag k0 = FragIO<TE>::load(Kn + (r + lead) * P, l);
+    const Frag v0 = FragIO<TE>::load(Vn + (r + lead) * P, l);
     if constexpr (LPR == 8) {
       // Reduce-scatter softmax: lanes 2k and 2k + 1 of the group hold the score of
       // source k; max, exponent and sum are formed once per source.
@@ -168,7 +178,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
       }
       const unsigned full = 0xffffffffu;
       const float val = group8_reduce_scatter4(x, l);
-      const bool live = src_has && pos >= src_off;
+      const bool live = src_has && pg >= src_off;
       const float sc = live ? val * c1 : -INFINITY;  // log2 units
       float m = fmaxf(sc, __shfl_xor_sync(full, sc, 2));
       m = fmaxf(m, __shfl_xor_sync(full, m, 4));
@@ -205,7 +215,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
       vf = FragIO<TE>::load(Vf + r * P, l);
     }
     // scores in log2 units: s * scale * log2(e)
-    const bool u0 = has0, u1 = has1 && pos >= 1, u2 = has2 && pos >= 2, uf = far && pos >= g.d;
+    const bool u0 = has0, u1 = has1 && pg >= 1, u2 = has2 && pg >= 2, uf = far && pg >= g.d;
     s0 = u0 ? s0 * c1 : -INFINITY;
     s1 = u1 ? s1 * c1 : -INFINITY;
     s2 = u2 ? s2 * c1 : -INFINITY;
@@ -235,25 +245,31 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
 // Backward
 // --------------------------------------------------------------------------
 
-// Issues the copies of one K/V slot: rows [p0, p0 + halo + T + halo).
-template <typename TE, int T, int P>
-__device__ __forceinline__ void tma_kv_slot(const BwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
+// Issues the copies of one K/V slot: rows [p0, p0 + halo + T + halo) of the
+// call's rows (p0 local).  Every box lies in one rank's shard (shards are tile
+// multiples, halos are shorter than a tile): pick_map gives its map and row.
+template <typename TE, int T, int P, typename Maps>
+__device__ __forceinline__ void tma_kv_slot(const Maps& maps, const BwdV2Params& p, uint64_t* bar,
                                             uint8_t* K, uint8_t* V, int p0, int halo, int h, int b) {
-  tma_rows(K, &maps.kH, bar, p.slots_k, p0, h, b);
-  tma_rows(V, &maps.vH, bar, p.slots_v, p0, h, b);
-  tma_rows(K + halo * P, &maps.kT, bar, p.slots_k, p0 + halo, h, b);
-  tma_rows(V + halo * P, &maps.vT, bar, p.slots_v, p0 + halo, h, b);
-  tma_rows(K + (halo + T) * P, &maps.kH, bar, p.slots_k, p0 + halo + T, h, b);
-  tma_rows(V + (halo + T) * P, &maps.vH, bar, p.slots_v, p0 + halo + T, h, b);
+  const int g0 = p.sh.pos0 + p0;
+  int c;
+  tma_rows(K, pick_map(maps.kH, p.sh, g0, c), bar, p.slots_k, c, h, b);
+  tma_rows(V, pick_map(maps.vH, p.sh, g0, c), bar, p.slots_v, c, h, b);
+  tma_rows(K + halo * P, pick_map(maps.kT, p.sh, g0 + halo, c), bar, p.slots_k, c, h, b);
+  tma_rows(V + halo * P, pick_map(maps.vT, p.sh, g0 + halo, c), bar, p.slots_v, c, h, b);
+  tma_rows(K + (halo + T) * P, pick_map(maps.kH, p.sh, g0 + halo + T, c), bar, p.slots_k, c, h, b);
+  tma_rows(V + (halo + T) * P, pick_map(maps.vH, p.sh, g0 + halo + T, c), bar, p.slots_v, c, h, b);
 }
 
-template <typename TE, int T, int P>
-__device__ __forceinline__ void tma_qd_slot(const BwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
+template <typename TE, int T, int P, typename Maps>
+__device__ __forceinline__ void tma_qd_slot(const Maps& maps, const BwdV2Params& p, uint64_t* bar,
                                             uint8_t* Q, uint8_t* Dd, int j0, int halo, int h, int b) {
-  tma_rows(Q, &maps.qT, bar, p.slots_q, j0, h, b);
-  tma_rows(Dd, &maps.dT, bar, p.slots_d, j0, h, b);
-  tma_rows(Q + T * P, &maps.qH, bar, p.slots_q, j0 + T, h, b);
-  tma_rows(Dd + T * P, &maps.dH, bar, p.slots_d, j0 + T, h, b);
+  const int g0 = p.sh.pos0 + j0;
+  int c;
+  tma_rows(Q, pick_map(maps.qT, p.sh, g0, c), bar, p.slots_q, c, h, b);
+  tma_rows(Dd, pick_map(maps.dT, p.sh, g0, c), bar, p.slots_d, c, h, b);
+  tma_rows(Q + T * P, pick_map(maps.qH, p.sh, g0 + T, c), bar, p.slots_q, c, h, b);
+  tma_rows(Dd + T * P, pick_map(maps.dH, p.sh, g0 + T, c), bar, p.slots_d, c, h, b);
 }
 
 // Source-set shapes the backward is compiled for.  0 reads the flags at run
@@ -272,8 +288,8 @@ struct BwdShape {
   static constexpr bool kLocalCarry = SHAPE == 3;
 };
 
-template <typename TE, int LPR, bool TMA, int SHAPE>
-__global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_constant__ BwdMaps maps,
+template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = BwdMaps>
+__global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_constant__ Maps maps,
                                                                   const BwdV2Params p) {
   constexpr int T = v2_tile(LPR);
   constexpr int P = LPR * FragIO<TE>::kLaneBytes;
@@ -312,15 +328,16 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
   h = bid % p.H;
   bid /= p.H;
   if (chain) {
-    const int r = bid % g.R;
-    bid /= g.R;
+    const int r = bid % g.chains;
+    bid /= g.chains;
     const int s = bid % g.segs;
     b = bid / g.segs;
     const int A_r = (g.nT - 1 - r) / g.R + 1;
     const int a_lo = s * g.seg;
     if (a_lo >= A_r) return;
     const int a_hi = min(a_lo + g.seg, A_r) - 1;
-    pre = a_hi + 1 < A_r;
+    // The tile above the segment may be on the next rank's shard (sharded calls).
+    pre = p.sh.pos0 / T + (a_hi + 1) * g.R + r < (p.sh.total_len + T - 1) / T;
     t_first = (a_hi + pre) * g.R + r;
     n_steps = a_hi - a_lo + 1 + pre;
     stride = g.R;
@@ -330,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     const int lo = s * g.seg;
     if (lo >= g.nT) return;
     const int hi = min(lo + g.seg, g.nT) - 1;
-    pre = lc && hi + 1 < g.nT;
+    pre = lc && p.sh.pos0 / T + hi + 1 < (p.sh.total_len + T - 1) / T;
     t_first = hi + pre;
     n_steps = hi - lo + 1 + pre;
     stride = 1;
@@ -377,10 +394,12 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
       uint64_t* bar = bars + (i & 1);
       mbar_arrive_expect_tx(bar, (uint32_t)((chain && i == 0 ? 2 : 1) * 2 * KVR * P));
       if (lc) {  // rows [j0 - d, j0 + T): a d-row box, then the tile
-        tma_rows(kslot(0), &maps.kH, bar, p.slots_k, j0 - d, h, b);
-        tma_rows(vslot(0), &maps.vH, bar, p.slots_v, j0 - d, h, b);
-        tma_rows(kslot(0) + d * P, &maps.kT, bar, p.slots_k, j0, h, b);
-        tma_rows(vslot(0) + d * P, &maps.vT, bar, p.slots_v, j0, h, b);
+        const int jg = p.sh.pos0 + j0;
+        int c;
+        tma_rows(kslot(0), pick_map(maps.kH, p.sh, jg - d, c), bar, p.slots_k, c, h, b);
+        tma_rows(vslot(0), pick_map(maps.vH, p.sh, jg - d, c), bar, p.slots_v, c, h, b);
+        tma_rows(kslot(0) + d * P, pick_map(maps.kT, p.sh, jg, c), bar, p.slots_k, c, h, b);
+        tma_rows(vslot(0) + d * P, pick_map(maps.vT, p.sh, jg, c), bar, p.slots_v, c, h, b);
       } else {
         for (int part = first; part < (chain ? 2 : 1); ++part) {
           const int slot = chain ? ((i + part) & 1) : 0;
@@ -415,7 +434,12 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
   const float scale = p.scale;
   const float c1 = scale * kLog2e;  // exp(a * scale - lse) = 2^(a * c1 - lse * log2 e)
   const long long bh = (long long)b * p.H + h;
-  const float* lse = p.lse + bh * p.L;
+  // log2-scaled LSE of consumer row j0 + c (local rows; past the shard end it is
+  // the next rank's row), 0 past the sequence.
+  auto lse_row = [&](int j0, int c) -> float {
+    const int qg = p.sh.pos0 + j0 + c;
+    return qg < p.sh.total_len ? lse_at(p.sh, bh, qg) * kLog2e : 0.f;
+  };
   TE* dq = reinterpret_cast<TE*>(const_cast<void*>(p.dq.ptr)) + (long long)b * p.dq.sb + (long long)h * p.dq.sh;
   TE* dk = reinterpret_cast<TE*>(const_cast<void*>(p.dk.ptr)) + (long long)b * p.dk.sb + (long long)h * p.dk.sh;
   TE* dv = reinterpret_cast<TE*>(const_cast<void*>(p.dv.ptr)) + (long long)b * p.dv.sb + (long long)h * p.dv.sh;
@@ -464,7 +488,8 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     // ---- Phase 1: softmax terms of every consumer, dQ of own queries. ----
     auto consume = [&](int c, bool act, float* erow, const Frag& k0, const Frag& v0, const Frag& k1,
                        const Frag& v1, const Frag& k2, const Frag& v2, float lq2) {
-      const int q = j0 + c;
+      const int q = j0 + c;             // local row (dQ store)
+      const int qg = p.sh.pos0 + q;     // global position (masks)
       const Frag qf = FragIO<TE>::load(Qs + c * P, l);
       const Frag df = FragIO<TE>::load(Ds + c * P, l);
       if constexpr (LPR == 8) {
@@ -487,8 +512,8 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
         }
         const unsigned full = 0xffffffffu;
         const float val = group8_reduce_scatter8(x, l);
-        const bool inr = q < p.L;
-        const bool live = l < 4 && src_has && inr && q >= src_off;
+        const bool inr = qg < p.sh.total_len;
+        const bool live = l < 4 && src_has && inr && qg >= src_off;
         const float pa = live ? fast_exp2(fmaf(val, c1, -lq2)) : 0.f;
         const float ps = __shfl_xor_sync(full, pa, 4);  // lanes 4..7: p of source l - 4
         const float t = l >= 4 ? ps * val : 0.f;
@@ -525,9 +550,9 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
         af = lane_group_sum<LPR>(frag_dot(qf, kf));
         bf = lane_group_sum<LPR>(frag_dot(df, vf));
       }
-      const bool inr = q < p.L;
-      const bool u0 = has0 && inr, u1 = has1 && inr && q >= 1, u2 = has2 && inr && q >= 2;
-      const bool uf = far && inr && q >= d;
+      const bool inr = qg < p.sh.total_len;
+      const bool u0 = has0 && inr, u1 = has1 && inr && qg >= 1, u2 = has2 && inr && qg >= 2;
+      const bool uf = far && inr && qg >= d;
       const float p0 = u0 ? fast_exp2(fmaf(a0, c1, -lq2)) : 0.f;
       const float p1 = u1 ? fast_exp2(fmaf(a1, c1, -lq2)) : 0.f;
       const float p2 = u2 ? fast_exp2(fmaf(a2, c1, -lq2)) : 0.f;
@@ -555,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
       const float* ls = LSEs + (step & 1) * p.lse_box;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        lq[i] = (TMA && p.lse_tma) ? ls[a + i] * kLog2e : ((j0 + a + i < p.L) ? lse[j0 + a + i] * kLog2e : 0.f);
+        lq[i] = (TMA && p.lse_tma) ? ls[a + i] * kLog2e : lse_row(j0, a + i);
       Frag k1 = FragIO<TE>::load(KN + (a + lead - 1) * P, l), k2 = FragIO<TE>::load(KN + (a + lead - 2) * P, l);
       Frag v1 = FragIO<TE>::load(VN + (a + lead - 1) * P, l), v2 = FragIO<TE>::load(VN + (a + lead - 2) * P, l);
       float* Eg = egroup(a);
@@ -592,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
           const bool act = e0 + i < Hc;
           const int c = act ? T + e0 + i : cbase;
           const float lq = (TMA && p.lse_tma) ? LSEs[(step & 1) * p.lse_box + c] * kLog2e
-                                              : ((act && j0 + c < p.L) ? lse[j0 + c] * kLog2e : 0.f);
+                                              : (act ? lse_row(j0, c) : 0.f);
           const Frag k0 = FragIO<TE>::load(KN + (c + lead) * P, l);
           const Frag v0 = FragIO<TE>::load(VN + (c + lead) * P, l);
           consume(c, act, erec(c), k0, v0, k1, v1, k2, v2, lq);
@@ -704,9 +729,9 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
 // Launchers
 // --------------------------------------------------------------------------
 
-template <typename TE, int LPR, bool TMA, int SHAPE>
-int launch_fwd_v2(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
-  auto kern = sbda_fwd_v2_kernel<TE, LPR, TMA, SHAPE>;
+template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps>
+int launch_fwd_v2(const Maps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  auto kern = sbda_fwd_v2_kernel<TE, LPR, TMA, SHAPE, Maps>;
   // The copy-engine path keeps Q out of shared memory.
   const size_t smem = pl.smem_fwd - (TMA ? (size_t)v2_tile(LPR) * pl.pitch : 0);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -716,17 +741,17 @@ int launch_fwd_v2(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, c
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
-template <typename TE, int LPR, bool TMA, int SHAPE>
-int launch_bwd_v2(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
-  auto kern = sbda_bwd_v2_kernel<TE, LPR, TMA, SHAPE>;
+template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps>
+int launch_bwd_v2(const Maps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+  auto kern = sbda_bwd_v2_kernel<TE, LPR, TMA, SHAPE, Maps>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
   kern<<<pl.blocks_bwd, kThreads, pl.smem_bwd, st>>>(maps, p);
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
-template <typename TE, bool TMA>
-int fwd_v2_lpr(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+template <typename TE, bool TMA, typename Maps>
+int fwd_v2_lpr(const Maps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
   if constexpr (TMA) {
     if (pl.lpr == 8) {
       const V2Geometry& g = pl.g;
@@ -751,8 +776,8 @@ int bwd_shape(const V2Geometry& g) {
   return 0;
 }
 
-template <typename TE, bool TMA>
-int bwd_v2_lpr(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+template <typename TE, bool TMA, typename Maps>
+int bwd_v2_lpr(const Maps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
   // Specialised shapes are compiled for the copy-engine path at 8 lanes per row.
   if constexpr (TMA) {
     if (pl.lpr == 8) {
@@ -774,15 +799,15 @@ int bwd_v2_lpr(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cuda
   return SBDA_ERR_UNSUPPORTED;
 }
 
-template <bool TMA>
-int fwd_v2_dtype(int dtype, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+template <bool TMA, typename Maps>
+int fwd_v2_dtype(int dtype, const Maps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
   if (dtype == SBDA_DTYPE_F32) return fwd_v2_lpr<float, TMA>(maps, p, pl, st);
   if (dtype == SBDA_DTYPE_F16) return fwd_v2_lpr<__half, TMA>(maps, p, pl, st);
   return fwd_v2_lpr<__nv_bfloat16, TMA>(maps, p, pl, st);
 }
 
-template <bool TMA>
-int bwd_v2_dtype(int dtype, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
+template <bool TMA, typename Maps>
+int bwd_v2_dtype(int dtype, const Maps& maps, const BwdV2Params& p, const V2Plan& pl, cudaStream_t st) {
   if (dtype == SBDA_DTYPE_F32) return bwd_v2_lpr<float, TMA>(maps, p, pl, st);
   if (dtype == SBDA_DTYPE_F16) return bwd_v2_lpr<__half, TMA>(maps, p, pl, st);
   return bwd_v2_lpr<__nv_bfloat16, TMA>(maps, p, pl, st);
@@ -795,6 +820,17 @@ int v2_forward(int dtype, bool tma, const FwdMaps& maps, const FwdV2Params& p, c
 int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
                 cudaStream_t st) {
   return tma ? bwd_v2_dtype<true>(dtype, maps, p, pl, st) : bwd_v2_dtype<false>(dtype, maps, p, pl, st);
+}
+
+// Sequence shards: one tensor map per rank, copy-engine layouts only.
+int v2_forward_sharded(int dtype, const ShardFwdMaps& maps, const FwdV2Params& p, const V2Plan& pl,
+                       cudaStream_t st) {
+  return fwd_v2_dtype<true>(dtype, maps, p, pl, st);
+}
+
+int v2_backward_sharded(int dtype, const ShardBwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
+                        cudaStream_t st) {
+  return bwd_v2_dtype<true>(dtype, maps, p, pl, st);
 }
 
 }  // namespace sbda

@@ -2,8 +2,9 @@
 
 1. Emulated ranks on one GPU: the sharded kernels see "rank r's buffer" only as an address,
    so W ranks are W slices of one sequence; one call per rank must reproduce the unsharded
-   op on the whole sequence.  Covers owner selection, near/far halos across shard ends,
-   global-position masks and remote LSE reads for W = 2, 4, 8.
+   op of the same kernel family on the whole sequence.  Covers owner selection, near/far
+   halos across shard ends, global-position masks and remote LSE reads for W = 2, 4, 8, on
+   the windowed and the general kernels.
 2. Two real ranks (two GPUs, two processes, NCCL + symmetric memory), when available.
 """
 
@@ -58,9 +59,9 @@ def _emulated(q, k, v, do, offsets, world):
     return out, dq, dk, dv
 
 
-def _whole(q, k, v, do, offsets):
-    """The unsharded general kernels on the whole sequence (same kernel family)."""
-    previous = _lib.set_kernel_path(1)
+def _whole(q, k, v, do, offsets, path=1):
+    """The unsharded kernels of family ``path`` (0 = auto, 1 = general) on the whole sequence."""
+    previous = _lib.set_kernel_path(path)
     try:
         out, lse = sbda_b200.sbda_forward(q, k, v, offsets)
         dq, dk, dv = sbda_b200.sbda_backward(q, k, v, do, lse, offsets)
@@ -69,18 +70,27 @@ def _whole(q, k, v, do, offsets):
     return out, dq, dk, dv
 
 
+@pytest.mark.parametrize("path", [0, 1], ids=["windowed", "general"])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_emulated_shards_match_whole_sequence(world):
+def test_emulated_shards_match_whole_sequence(world, path):
+    """Sharded calls equal the same kernel family on the whole sequence, bit for bit: the
+    windowed kernels (chain walks whose far tiles, pre tiles and halos come from other shards;
+    local and local-carry walks across shard ends; a far offset longer than a shard) and the
+    general kernels."""
     total = 8 * 1024
     g = torch.Generator(device="cuda").manual_seed(world)
     make = lambda h: torch.randn(1, total, h, 64, device="cuda", generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)  # noqa: E731
     q, k, v, do = make(4), make(4), make(4), make(4)
-    for layer in (1, 2, 3, 7, 8, 10, 11, 12, 13, 14):
-        offsets = sbda_b200.topology_offsets(layer)
-        got = _emulated(q, k, v, do, offsets, world)
-        ref = _whole(q, k, v, do, offsets)
-        for name, a, b in zip(("O", "dQ", "dK", "dV"), got, ref):
-            assert torch.equal(a, b), f"layer {layer} world {world}: {name} differs"
+    previous = _lib.set_kernel_path(path)
+    try:
+        for layer in (1, 2, 3, 5, 6, 7, 8, 10, 11, 12, 13, 14):
+            offsets = sbda_b200.topology_offsets(layer)
+            got = _emulated(q, k, v, do, offsets, world)
+            ref = _whole(q, k, v, do, offsets, path)
+            for name, a, b in zip(("O", "dQ", "dK", "dV"), got, ref):
+                assert torch.equal(a, b), f"layer {layer} world {world}: {name} differs"
+    finally:
+        _lib.set_kernel_path(previous)
     assert sbda_b200.device_status(reset=True) == 0
 
 
@@ -132,7 +142,7 @@ def _two_rank_worker(rank: int, world: int, port: int, result: "torch.multiproce
             dq, dk, dv = sharded_backward(q, k, v, do, lse, offsets, shards)
             shards.barrier()
             whole = [t.permute(0, 2, 1, 3) for t in full]
-            ref = _whole(*whole, offsets)
+            ref = _whole(*whole, offsets, 0)
             for a, b in zip((out, dq, dk, dv), ref):
                 ok &= bool(torch.equal(a, b[:, :, lo:hi]))
         torch.cuda.synchronize()
