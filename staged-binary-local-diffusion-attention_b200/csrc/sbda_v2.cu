@@ -35,6 +35,11 @@
 //  * The softmax records of a step live in a ring of two tiles: in a walk of
 //    consecutive tiles the consumers past this tile's end are the first rows
 //    of the previous step's tile, so only the first step computes them.
+//  * Sequence shards: a call covers one rank's rows; every TMA box lies in one
+//    rank's shard (tiles, in-tile halos, d-aligned chain tiles), so the box's
+//    map is the owner's (pick_map).  Masks use global positions, LSE rows past
+//    the shard are read from their owner, and a walk's pre tile may be the next
+//    rank's.  One shard (pos0 = 0, total_len = L) is the unsharded case.
 
 #include <type_traits>
 
