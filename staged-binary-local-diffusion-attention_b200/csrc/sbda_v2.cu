@@ -67,7 +67,8 @@ __device__ __forceinline__ int chain_tile_v2(int idx, int R, int A, int rem) {
 // --------------------------------------------------------------------------
 
 // Source-set shapes of the forward: 0 = flags read at run time, 1 = {0, 1},
-// 2 = {0, 2}, 3 = {0, 1, 2, d}.
+// 2 = {0, 2}, 3 = {0, 1, 2, d} with d >= TILE (own far tile), 4 = {0, 1, 2, d}
+// with d < TILE (one window).
 template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = FwdMaps>
 __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_constant__ Maps maps,
                                                                const FwdV2Params p) {
@@ -84,9 +85,9 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   const int t = chain_tile_v2(bid % g.nT, g.R, g.A, g.rem);
   const int b = bid / g.nT;
   const int i0 = t * T;
-  const bool has1 = SHAPE == 0 ? g.has1 != 0 : (SHAPE == 1 || SHAPE == 3);
+  const bool has1 = SHAPE == 0 ? g.has1 != 0 : (SHAPE == 1 || SHAPE >= 3);
   const bool has2 = SHAPE == 0 ? g.has2 != 0 : SHAPE >= 2;
-  const bool far = SHAPE == 0 ? g.has_far != 0 : SHAPE == 3;
+  const bool far = SHAPE == 0 ? g.has_far != 0 : SHAPE >= 3;
   const bool has0 = SHAPE == 0 ? g.has0 != 0 : true;
 
   // The copy-engine path reads each group's Q rows straight into registers
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   // offset is shorter than a tile -- its sources then lie in the same window
   // (staged once, as a d-row box and the tile, both tile-aligned).  A far offset
   // of a tile or more gets its own tile [i0 - d, i0 - d + T).
-  const bool near_far = far && g.d < T;
+  const bool near_far = SHAPE == 0 ? far && g.d < T : SHAPE == 4;
   const int lead = near_far ? g.d : 2;
   uint8_t* Qs = smem;
   uint8_t* Kn = smem + (TMA ? 0 : T * P);
@@ -762,7 +763,8 @@ int fwd_v2_lpr(const Maps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStr
       const V2Geometry& g = pl.g;
       if (g.has0 && g.has1 && !g.has2 && !g.has_far) return launch_fwd_v2<TE, 8, TMA, 1>(maps, p, pl, st);
       if (g.has0 && !g.has1 && g.has2 && !g.has_far) return launch_fwd_v2<TE, 8, TMA, 2>(maps, p, pl, st);
-      if (g.has0 && g.has1 && g.has2 && g.has_far) return launch_fwd_v2<TE, 8, TMA, 3>(maps, p, pl, st);
+      if (g.has0 && g.has1 && g.has2 && g.has_far)
+        return g.d < pl.tile ? launch_fwd_v2<TE, 8, TMA, 4>(maps, p, pl, st) : launch_fwd_v2<TE, 8, TMA, 3>(maps, p, pl, st);
     }
   }
   if constexpr (sizeof(TE) == 4) {
