@@ -3,8 +3,9 @@
 Rank ``r`` of a process group holds positions ``[r * L, (r + 1) * L)`` of one sequence (the
 reference runs one sequence on one GPU; long sequences are its scaling axis, SURVEY config 5).
 A query's dyadic source ``i - d`` and a key's dyadic consumer ``j + d`` may live on another
-rank: the kernels stage those rows per tile straight from the owning GPU's buffer over
-NVLink (non-multicast TMA loads of peer memory).  The buffers peers read are allocated in
+rank: the kernels (the windowed ones for SBDA schedules, the general ones otherwise) stage those
+rows per tile straight from the owning GPU's buffer over NVLink (non-multicast TMA loads of peer
+memory).  One rank (world 1) runs the unsharded kernels.  The buffers peers read are allocated in
 symmetric memory (``torch.distributed._symmetric_memory``) so every rank can address every
 other rank's copy; NCCL / the process group is used only to exchange handles and for the
 device-side barrier that orders a layer's writes before its peers' reads.
