@@ -34,6 +34,7 @@ import torch  # noqa: E402
 METRIC = "SBDA attn fwd+bwd Mpositions/s at 1M×20L; % of B200 HBM roofline"
 UNIT = "Mpositions/s"
 FALLBACK_HBM_GBS = 6650.0
+PEER_LINK_GBS = 770.0  # measured peer copy per direction on this pool (nominal 900)
 
 
 def parse_args():
@@ -92,6 +93,41 @@ def profiled_traffic() -> float | None:
     except OSError:
         pass
     return None
+
+
+def shard_link_model(total: int, world: int, heads: int, head_dim: int, elem: int, offsets_per_layer,
+                     hbm_gbs: float, link_gbs: float = PEER_LINK_GBS) -> dict:
+    """Bytes that must cross NVLink in one fwd+bwd step of contiguous sequence shards, and the
+    step time they allow.
+
+    Per layer with far offset d, rank r (shard [a, a + S)) reads from other ranks:
+      * forward and backward: K and V of the far sources of its rows i with 0 <= i - d < a
+        (2 * D * e bytes per row and head, once in each pass);
+      * backward: for its keys j whose far consumer j + d lies past its shard (and inside the
+        sequence), that consumer's Q, dO, K, V and LSE (4 * D * e + 4 bytes), because the far
+        consumers of a rank's keys are recomputed on the key's rank.
+    The 1- and 2-row near halos at shard ends are left out (under 0.01 % of the bytes).  A layer
+    takes at least max(local algorithmic bytes / HBM peak, remote bytes / link bandwidth) on each
+    rank; the step target is the sum over layers of the slowest rank's bound.
+    """
+    shard = total // world
+    local = shard * heads * (11 * head_dim * elem + 8)
+    worst_remote, target_s = 0, 0.0
+    for offsets in offsets_per_layer:
+        d = max(offsets)
+        if d < 3:
+            target_s += local / (hbm_gbs * 1e9)
+            continue
+        layer_bound = 0.0
+        for rank in range(world):
+            a = rank * shard
+            far_rows = max(0, min(a + shard, a + d) - max(a, d))
+            consumer_rows = max(0, min(a + shard, total - d) - max(a, a + shard - d))
+            remote = heads * (2 * far_rows * 2 * head_dim * elem + consumer_rows * (4 * head_dim * elem + 4))
+            worst_remote = max(worst_remote, remote)
+            layer_bound = max(layer_bound, local / (hbm_gbs * 1e9), remote / (link_gbs * 1e9))
+        target_s += layer_bound
+    return {"link_gbs": link_gbs, "max_remote_bytes_one_layer": worst_remote, "target_ms": target_s * 1e3}
 
 
 class ClockSampler:
@@ -470,12 +506,14 @@ def run_seqshard(args) -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    sampler = ClockSampler(local)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
         step()
     end.record()
     torch.cuda.synchronize()
+    clocks = sampler.stop()
     ms = start.elapsed_time(end) / args.steps
     if world > 1:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
@@ -483,6 +521,8 @@ def run_seqshard(args) -> None:
         ms = float(t.item())
     peak, peak_kind = measured_peak_gbs()
     step_bytes = total * H * layers * (11 * D * 2 + 8)
+    link = shard_link_model(total, world, H, D, 2, offsets, peak)
+    link["frac_of_target"] = link["target_ms"] / ms
     if rank == 0:
         print(json.dumps({
             "metric": "SBDA attn fwd+bwd Mpositions/s, one 4M-position sequence x 22 layers in contiguous shards",
@@ -491,8 +531,11 @@ def run_seqshard(args) -> None:
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded, resident in HBM",
             "config": {"workload": f"cfg5: {total} positions x {layers} layers, {H} heads x {D}, "
                                    f"{world} contiguous shards of {shard}",
-                       "kernels": "general (sbda_v1) sharded kernels; dyadic halos staged from the owning GPU "
-                                  "over NVLink with non-multicast TMA"},
+                       "kernels": ("windowed (sbda_v2) kernels; 1 GPU: unsharded calls; N > 1: sharded calls "
+                                   "whose K/V tiles and halos past the shard are staged from the owning GPU over "
+                                   "NVLink with non-multicast TMA")},
+            "clocks": clocks,
+            "shard_link_model": link,
             "step_roofline": {"achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": peak * world, "unit": "GB/s",
                               "frac": step_bytes / (ms * 1e-3) / 1e9 / (peak * world), "peak_kind": peak_kind,
                               "algorithmic_bytes_per_step": step_bytes},

@@ -62,3 +62,36 @@ def test_shard_bounds_validation():
     with pytest.raises(ValueError):
         owner_of(10, 10, 2)
     assert torch.tensor([shard_bounds(8, 4, r)[0] for r in range(4)]).tolist() == [0, 2, 4, 6]
+
+
+def test_shard_link_model_counts_remote_rows():
+    """The NVLink byte model of the config-5 bench line equals a row-by-row count: far K/V
+    sources on other ranks (forward and backward) and far consumers past the shard end
+    (backward: their Q, dO, K, V and LSE)."""
+    import bench
+    from sbda_b200 import sbda_layer_offsets
+
+    total, heads, dim, elem = 2048, 2, 16, 2
+    for world in (1, 2, 4, 8):
+        shard = total // world
+        layers = sbda_layer_offsets(11)
+        model = bench.shard_link_model(total, world, heads, dim, elem, layers, hbm_gbs=1.0, link_gbs=1.0)
+        worst, target = 0, 0.0
+        local = shard * heads * (11 * dim * elem + 8)
+        for offsets in layers:
+            d = max(offsets)
+            bound = local
+            for rank in range(world):
+                lo, hi = shard_bounds(total, world, rank)
+                remote = 0
+                if d >= 3:
+                    for i in range(lo, hi):
+                        if 0 <= i - d < lo:
+                            remote += 2 * heads * 2 * dim * elem
+                        if hi <= i + d < total:
+                            remote += heads * (4 * dim * elem + 4)
+                worst = max(worst, remote)
+                bound = max(bound, remote)
+            target += bound
+        assert model["max_remote_bytes_one_layer"] == worst
+        assert abs(model["target_ms"] - target * 1e-6) < 1e-9 * target
