@@ -114,7 +114,9 @@ int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int3
  * single-GPU; SURVEY row "sequence shards").  Rank r of `world` (<= 8) holds
  * positions [r*L, (r+1)*L) of one sequence, L = shape.length, the same on
  * every rank and a multiple of the tile height (64 for 16-bit D <= 64).  The
- * far offset, if any, must also be a tile multiple.  k_ranks[i] / v_ranks[i]
+ * far offset, if any, must also be a tile multiple, or shorter than a tile
+ * where the windowed kernels serve the offsets (near offsets within {0,1,2},
+ * heads == kv_heads; the default kernel path).  k_ranks[i] / v_ranks[i]
  * (and in the backward q, grad_out, lse) describe rank i's buffers as
  * addresses valid on this GPU (peer memory mapped into this process, e.g.
  * CUDA IPC or symmetric memory); the kernels stage remote rows over NVLink
