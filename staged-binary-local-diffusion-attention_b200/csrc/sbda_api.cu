@@ -623,6 +623,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
     memset(&maps, 0, sizeof(maps));
     bool tma = vec;
     p.lse_box = p2.lse_box;
+    p.lse_tx = p2.lse_box * 4;
     if (tma) {
       unsigned dummy;
       const int hz = p2.g.halo;
@@ -903,7 +904,6 @@ extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int
       p.dv = arg_of(grad_v);
       p.lse = lse_ranks[rank];
       p.status = status_ptr();
-      p.lse_tma = 0;  // LSE rows past the shard end are the next rank's: read per row
       p.lse_box = p2.lse_box;
       p.sh = shard_info(rank, world, Ls);
       for (int r = 0; r < world; ++r) p.sh.lse[r] = lse_ranks[r];
@@ -911,6 +911,14 @@ extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int
       const int lead = p2.g.mode == 2 ? p2.g.d : hz;
       ShardBwdMaps maps;
       memset(&maps, 0, sizeof(maps));
+      // LSE rows by the copy engine: the tile's rows and the halo rows past it
+      // (rounded up to 16 bytes), each box from its owner; else per-row loads.
+      const int lse_halo = (hz + 3) / 4 * 4;
+      p.lse_tma = 1;
+      p.lse_tx = (p2.tile + lse_halo) * 4;
+      for (int r = 0; r < world && p.lse_tma; ++r)
+        p.lse_tma = encode_lse_map(&maps.lseT[r], lse_ranks[r], B * H, Ls, p2.tile) &&
+                    encode_lse_map(&maps.lseH[r], lse_ranks[r], B * H, Ls, lse_halo);
       if (encode_ranks(maps.qT, &p.slots_q, q_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
           encode_ranks(maps.dT, &p.slots_d, grad_out_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&
           encode_ranks(maps.kT, &p.slots_k, k_ranks, world, dtype, B, H, Ls, D, p2.pitch, p2.tile) &&

@@ -90,7 +90,9 @@ struct ShardFwdMaps {
 struct ShardBwdMaps {
   CUtensorMap qT[kMaxShards], qH[kMaxShards], dT[kMaxShards], dH[kMaxShards];
   CUtensorMap kT[kMaxShards], kH[kMaxShards], vT[kMaxShards], vH[kMaxShards];
-  CUtensorMap lseT;  // unused: sharded calls read LSE rows through ShardInfo::lse
+  // LSE rows (fp32 [B*H, L] per rank): lseT boxes one tile, lseH the halo rows
+  // past it (rounded up to 4), each from the rank that owns them.
+  CUtensorMap lseT[kMaxShards], lseH[kMaxShards];
 };
 
 // Map and map coordinate of the rows starting at global position gpos.
@@ -601,7 +603,8 @@ struct BwdV2Params {
   unsigned slots_q, slots_k, slots_v, slots_d;
   unsigned* status;
   int lse_tma;   // 1: LSE rows staged by the copy engine with Q/dO (L % 4 == 0)
-  int lse_box;   // rows of that box (Q/dO slot height rounded up to 32)
+  int lse_box;   // rows of an LSE slot in shared memory (Q/dO slot height rounded up to 32)
+  int lse_tx;    // bytes the LSE copies of one step deliver
   ShardInfo sh;  // one shard (pos0 = 0, total_len = L) unless sequence-sharded
 };
 

@@ -278,6 +278,26 @@ __device__ __forceinline__ void tma_qd_slot(const Maps& maps, const BwdV2Params&
   tma_rows(Dd + T * P, pick_map(maps.dH, p.sh, g0 + T, c), bar, p.slots_d, c, h, b);
 }
 
+// LSE rows of a Q/dO slot (the tile and the consumers past it).  One GPU: one
+// box of lse_box rows.  Shards: the tile's rows from this rank and the halo
+// rows from their owner (past the sequence end: this rank's map out of range,
+// zero-filled); both boxes start at tile-aligned rows.
+template <int T>
+__device__ __forceinline__ void tma_lse_slot(const BwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
+                                             float* dst, int j0, int row) {
+  tma_2d(dst, &maps.lseT, bar, j0, row);
+}
+template <int T>
+__device__ __forceinline__ void tma_lse_slot(const ShardBwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
+                                             float* dst, int j0, int row) {
+  const int g0 = p.sh.pos0 + j0;
+  int c;
+  const CUtensorMap* m = pick_map(maps.lseT, p.sh, g0, c);
+  tma_2d(dst, m, bar, c, row);
+  m = pick_map(maps.lseH, p.sh, g0 + T, c);
+  tma_2d(dst + T, m, bar, c, row);
+}
+
 // Source-set shapes the backward is compiled for.  0 reads the flags at run
 // time; the others fix them so the per-row code is straight-line:
 //   1: {0, 1} (SBDA layer 1)          2: {0, 2} (SBDA layer 2)
@@ -382,9 +402,9 @@ __global__ void __launch_bounds__(kThreads, 3) sbda_bwd_v2_kernel(const __grid_c
     const int j0 = (t_first - i * stride) * T;
     if constexpr (TMA) {
       uint64_t* bar = bars + (i & 1);
-      mbar_arrive_expect_tx(bar, (uint32_t)(2 * QDR * P + (p.lse_tma ? p.lse_box * 4 : 0)));
+      mbar_arrive_expect_tx(bar, (uint32_t)(2 * QDR * P + (p.lse_tma ? p.lse_tx : 0)));
       tma_qd_slot<TE, T, P>(maps, p, bar, qslot(i & 1), dslot(i & 1), j0, Hc, h, b);
-      if (p.lse_tma) tma_2d(LSEs + (i & 1) * p.lse_box, &maps.lseT, bar, j0, b * p.H + h);
+      if (p.lse_tma) tma_lse_slot<T>(maps, p, bar, LSEs + (i & 1) * p.lse_box, j0, b * p.H + h);
     } else {
       constexpr int PE = P / sizeof(TE);
       generic_rows<TE>(qslot(i & 1), p.q, b, h, j0, QDR, p.L, p.D, PE);
