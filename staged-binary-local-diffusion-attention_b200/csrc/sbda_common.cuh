@@ -106,8 +106,15 @@ __device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap& m, con
 }
 __device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap (&m)[kMaxShards], const ShardInfo& s,
                                                        int gpos, int& coord) {
+  // Most boxes are this rank's rows: one compare.  Otherwise the owner is the
+  // number of shard starts at or below gpos (no integer division on the path
+  // that issues the copies).
   int owner = s.rank;
-  if (gpos >= 0 && gpos < s.total_len) owner = gpos / s.shard_len;
+  if ((unsigned)(gpos - s.pos0) >= (unsigned)s.shard_len && gpos >= 0 && gpos < s.total_len) {
+    owner = 0;
+#pragma unroll
+    for (int r = 1; r < kMaxShards; ++r) owner += gpos >= (long long)r * s.shard_len ? 1 : 0;
+  }
   coord = gpos - owner * s.shard_len;
   return &m[owner];
 }
