@@ -35,6 +35,10 @@ METRIC = "SBDA attn fwd+bwd Mpositions/s at 1M×20L; % of B200 HBM roofline"
 UNIT = "Mpositions/s"
 FALLBACK_HBM_GBS = 6650.0
 PEER_LINK_GBS = 770.0  # measured peer copy per direction on this pool (nominal 900)
+# CPU sample length of both CPU legs (the cpu_baseline object and --impl reference): 65,536
+# positions with every layer's offsets; the gather path is O(L) per layer, so positions/s carries
+# over to 1M.  At 65,536 positions every layer up to 2^15 has live far sources.
+CPU_SAMPLE_POSITIONS = 65536
 
 
 def parse_args():
@@ -55,7 +59,7 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-sample-length", type=int, default=16384)
+    p.add_argument("--cpu-sample-length", type=int, default=CPU_SAMPLE_POSITIONS)
     return p.parse_args()
 
 
@@ -70,6 +74,7 @@ def workload_config(args, world: int) -> dict:
         "head_dim": args.head_dim,
         "parallelism": f"batch-sharded x{world} (independent sequences, no collectives)",
         "l2": "every tensor 512 MiB > 126 MB L2; no flush needed",
+        "cpu_sample_positions": args.cpu_sample_length,
     }
 
 
@@ -208,7 +213,7 @@ def run_reference(args) -> None:
     from oracle import sbda_oracle as orc
 
     torch.set_num_threads(os.cpu_count() or 1)
-    sample = 2048
+    sample = args.cpu_sample_length
     g = torch.Generator().manual_seed(7)
     shape = (1, args.heads, sample, args.head_dim)
     q, k, v, do = (torch.randn(shape, generator=g) for _ in range(4))

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define SBDA_B200_ABI_VERSION 1
+#define SBDA_B200_ABI_VERSION 2
 
 /* Element types (match the reference's accepted dtypes, sbda_triton.py:1302-1303). */
 enum sbda_dtype {
@@ -110,8 +110,8 @@ int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int3
                        void* stream);
 
 /*
- * Contiguous sequence shards (no counterpart in the reference, which is
- * single-GPU; SURVEY row "sequence shards").  Rank r of `world` (<= 8) holds
+ * Contiguous sequence shards (no counterpart in the reference, which runs
+ * one sequence on one GPU).  Rank r of `world` (<= 8) holds
  * positions [r*L, (r+1)*L) of one sequence, L = shape.length, the same on
  * every rank and a multiple of the tile height (64 for 16-bit D <= 64).  The
  * far offset, if any, must also be a tile multiple, or shorter than a tile
@@ -275,14 +275,34 @@ int sbda_b200_silu_mul_backward(int dtype, int64_t n, const void* gate, const vo
                                 const void* grad_h, void* grad_gate, void* grad_up, void* stream);
 
 /*
- * Process-wide kernel selection, for tests and benchmarks: 0 = automatic
- * (the windowed chain-walking kernels wherever they apply, else the general
- * ones, else the uniform ones), 1 = general kernels (uniform ones for offset
- * sets with several far offsets), 2 = uniform kernels only.  Returns the
- * previous setting, or -1 for an unknown value.  All families compute the
- * same function.
+ * The same four calls with the kernel family chosen by the caller, for tests
+ * and benchmarks that compare the families (no counterpart in the reference,
+ * which has one Triton kernel set).  family: 0 = automatic (what the calls
+ * above do: the windowed chain-walking kernels wherever they apply, else the
+ * general ones, else the uniform ones), 1 = general kernels (uniform ones for
+ * offset sets with several far offsets), 2 = uniform kernels (sharded calls:
+ * treated as 1).  Any other value returns SBDA_ERR_INVALID.  All families
+ * compute the same function; their fp32 rounding differs, so a backward
+ * should use the family its forward used.  The choice is an argument: the
+ * library keeps no process-wide kernel setting.
  */
-int sbda_b200_set_kernel_path(int path);
+int sbda_b200_forward_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                         float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v, sbda_tensor out, float* lse,
+                         void* stream);
+int sbda_b200_backward_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                          float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v, sbda_tensor grad_out,
+                          const float* lse, sbda_tensor grad_q, sbda_tensor grad_k, sbda_tensor grad_v,
+                          void* stream);
+int sbda_b200_forward_sharded_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets,
+                                 int32_t n_offsets, float scale, int32_t rank, int32_t world, sbda_tensor q,
+                                 const sbda_tensor* k_ranks, const sbda_tensor* v_ranks, sbda_tensor out,
+                                 float* lse, void* stream);
+int sbda_b200_backward_sharded_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets,
+                                  int32_t n_offsets, float scale, int32_t rank, int32_t world,
+                                  const sbda_tensor* q_ranks, const sbda_tensor* k_ranks,
+                                  const sbda_tensor* v_ranks, const sbda_tensor* grad_out_ranks,
+                                  const float* const* lse_ranks, sbda_tensor grad_q, sbda_tensor grad_k,
+                                  sbda_tensor grad_v, void* stream);
 
 /*
  * Reads (and, if reset != 0, clears) the calling device's fault word that

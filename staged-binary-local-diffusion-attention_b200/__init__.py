@@ -6,6 +6,7 @@ from ``csrc/`` by ``build.py``) behind the C ABI of ``include/sbda_b200.h``.
 """
 
 from .ops import (
+    current_family,
     device_status,
     fused_sbda,
     fused_sbda_block,
@@ -13,6 +14,7 @@ from .ops import (
     fused_sbda_gqa_key_backward,
     fused_sbda_key_backward,
     host_offsets,
+    kernel_family,
     sbda_attention,
     sbda_backward,
     sbda_forward,
@@ -22,7 +24,7 @@ from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_
 
 __all__ = [
     "BiAttnBlock", "BinaryPathAttention", "PATH_TOPOLOGIES", "RMSNorm", "SBDAttention", "SwiGLU",
-    "add_rms_norm", "rms_norm", "silu_mul", "SBDAAttention", "device_status", "fused_sbda",
+    "add_rms_norm", "rms_norm", "silu_mul", "SBDAAttention", "current_family", "device_status", "kernel_family", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
     "fused_sbda_key_backward", "host_offsets", "norm_rope", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
     "sbda_layer_offsets", "sbda_stage", "topology_offsets",

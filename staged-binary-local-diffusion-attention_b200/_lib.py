@@ -159,8 +159,16 @@ def load() -> ctypes.CDLL:
             tarr, tarr, tarr, tarr, ctypes.POINTER(c_void_p),
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
-        lib.sbda_b200_set_kernel_path.restype = c_int
-        lib.sbda_b200_set_kernel_path.argtypes = [c_int]
+        fwd_args = lib.sbda_b200_forward.argtypes
+        bwd_args = lib.sbda_b200_backward.argtypes
+        lib.sbda_b200_forward_ex.restype = c_int
+        lib.sbda_b200_forward_ex.argtypes = [c_int] + list(fwd_args)
+        lib.sbda_b200_backward_ex.restype = c_int
+        lib.sbda_b200_backward_ex.argtypes = [c_int] + list(bwd_args)
+        lib.sbda_b200_forward_sharded_ex.restype = c_int
+        lib.sbda_b200_forward_sharded_ex.argtypes = [c_int] + list(lib.sbda_b200_forward_sharded.argtypes)
+        lib.sbda_b200_backward_sharded_ex.restype = c_int
+        lib.sbda_b200_backward_sharded_ex.argtypes = [c_int] + list(lib.sbda_b200_backward_sharded.argtypes)
         lib.sbda_b200_device_status.restype = c_int
         lib.sbda_b200_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), c_int]
         _lib = lib
@@ -190,13 +198,18 @@ def offsets_array(offsets: tuple[int, ...]):
     return array
 
 
-def set_kernel_path(path: int) -> int:
-    """0 = automatic, 1 = general kernels (uniform ones where those cannot serve the offsets),
-    2 = uniform kernels only (process-wide); returns the previous value."""
-    previous = load().sbda_b200_set_kernel_path(int(path))
-    if previous < 0:
-        raise ValueError(f"unknown kernel path {path}")
-    return previous
+KERNEL_FAMILIES = {"auto": 0, "general": 1, "uniform": 2}
+
+
+def family_code(family: str | int) -> int:
+    """Kernel family name (or code) -> the ``family`` argument of the ``*_ex`` entry points."""
+    if isinstance(family, str):
+        if family not in KERNEL_FAMILIES:
+            raise ValueError(f"unknown kernel family {family!r}")
+        return KERNEL_FAMILIES[family]
+    if int(family) not in KERNEL_FAMILIES.values():
+        raise ValueError(f"unknown kernel family {family}")
+    return int(family)
 
 
 def device_status(reset: bool = True) -> int:

@@ -27,7 +27,10 @@ unsigned* status_ptr() {
   return static_cast<unsigned*>(addr);
 }
 
-std::atomic<int> g_kernel_path{0};  // 0 = automatic, 1 = general kernels, 2 = uniform kernels
+// Kernel families a call may be pinned to (the *_ex entry points): 0 = automatic,
+// 1 = general kernels, 2 = uniform kernels.  There is no process-wide setting.
+constexpr int kFamilyAuto = 0, kFamilyGeneral = 1, kFamilyUniform = 2;
+bool family_ok(int family) { return family >= kFamilyAuto && family <= kFamilyUniform; }
 
 int sm_count() {
   int dev = 0, n = 148;
@@ -498,14 +501,10 @@ extern "C" const char* sbda_b200_status_string(int status) {
   }
 }
 
-extern "C" int sbda_b200_set_kernel_path(int path) {
-  if (path < 0 || path > 2) return -1;
-  return g_kernel_path.exchange(path);
-}
-
-extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
-                                 float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v, sbda_tensor out,
-                                 float* lse, void* stream) {
+extern "C" int sbda_b200_forward_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets,
+                                    int32_t n_offsets, float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                    sbda_tensor out, float* lse, void* stream) {
+  if (!family_ok(family)) return SBDA_ERR_INVALID;
   int st = validate(dtype, shape, offsets, n_offsets);
   if (st != SBDA_OK) return st;
   const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
@@ -516,7 +515,7 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
   const bool vec = tensors_vector_ok({&q, &k, &v, &out}, B, L, D, e, {H, Hkv, Hkv, H});
 
   V2Plan p2;
-  if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
+  if (family == kFamilyAuto && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
     FwdV2Params p;
     memset(&p, 0, sizeof(p));
     p.B = (int)B;
@@ -547,7 +546,7 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
   }
 
   Plan pl;
-  st = g_kernel_path.load() == 2 ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
+  st = family == kFamilyUniform ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
   if (st == SBDA_ERR_UNSUPPORTED)  // several far offsets (or forced): the uniform kernels
     return uniform_forward(dtype, shape, offsets, n_offsets, scale, q, k, v, nullptr, out, lse, vec, s);
   if (st != SBDA_OK) return st;
@@ -583,10 +582,17 @@ extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* off
   return v1_forward(dtype, tma, maps, p, pl, s);
 }
 
-extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
-                                  float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
-                                  sbda_tensor grad_out, const float* lse, sbda_tensor grad_q,
-                                  sbda_tensor grad_k, sbda_tensor grad_v, void* stream) {
+extern "C" int sbda_b200_forward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                 float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v, sbda_tensor out,
+                                 float* lse, void* stream) {
+  return sbda_b200_forward_ex(kFamilyAuto, dtype, shape, offsets, n_offsets, scale, q, k, v, out, lse, stream);
+}
+
+extern "C" int sbda_b200_backward_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets,
+                                     int32_t n_offsets, float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                     sbda_tensor grad_out, const float* lse, sbda_tensor grad_q,
+                                     sbda_tensor grad_k, sbda_tensor grad_v, void* stream) {
+  if (!family_ok(family)) return SBDA_ERR_INVALID;
   int st = validate(dtype, shape, offsets, n_offsets);
   if (st != SBDA_OK) return st;
   const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
@@ -600,7 +606,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
                                      {H, Hkv, Hkv, H, H, Hkv, Hkv});
 
   V2Plan p2;
-  if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
+  if (family == kFamilyAuto && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
     BwdV2Params p;
     memset(&p, 0, sizeof(p));
     p.B = (int)B;
@@ -642,7 +648,7 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
   }
 
   Plan pl;
-  st = g_kernel_path.load() == 2 ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
+  st = family == kFamilyUniform ? SBDA_ERR_UNSUPPORTED : make_plan(offsets, n_offsets, L, D, e, &pl);
   if (st == SBDA_ERR_UNSUPPORTED)  // several far offsets (or forced): the uniform kernels
     return uniform_backward(dtype, shape, offsets, n_offsets, scale, q, k, v, nullptr, grad_out, lse, grad_q,
                             grad_k, grad_v, vec, s);
@@ -683,6 +689,14 @@ extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* of
             encode_map(&maps.vH, &dummy, v, dtype, B, Hkv, L, D, pl.pitch, pl.g.Hn);
   }
   return v1_backward(dtype, tma, maps, p, pl, s);
+}
+
+extern "C" int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                  float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                  sbda_tensor grad_out, const float* lse, sbda_tensor grad_q,
+                                  sbda_tensor grad_k, sbda_tensor grad_v, void* stream) {
+  return sbda_b200_backward_ex(kFamilyAuto, dtype, shape, offsets, n_offsets, scale, q, k, v, grad_out, lse,
+                               grad_q, grad_k, grad_v, stream);
 }
 
 extern "C" int sbda_b200_forward_masked(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
@@ -779,10 +793,11 @@ bool encode_ranks(CUtensorMap* maps, unsigned* slots, const sbda_tensor* ts, int
 
 }  // namespace sbda
 
-extern "C" int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
-                                         float scale, int32_t rank, int32_t world, sbda_tensor q,
-                                         const sbda_tensor* k_ranks, const sbda_tensor* v_ranks, sbda_tensor out,
-                                         float* lse, void* stream) {
+extern "C" int sbda_b200_forward_sharded_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets,
+                                            int32_t n_offsets, float scale, int32_t rank, int32_t world,
+                                            sbda_tensor q, const sbda_tensor* k_ranks, const sbda_tensor* v_ranks,
+                                            sbda_tensor out, float* lse, void* stream) {
+  if (!family_ok(family)) return SBDA_ERR_INVALID;
   int st = validate(dtype, shape, offsets, n_offsets);
   if (st != SBDA_OK) return st;
   if (world < 1 || world > kMaxShards || rank < 0 || rank >= world || !k_ranks || !v_ranks)
@@ -793,12 +808,14 @@ extern "C" int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int3
   for (int r = 0; r < world; ++r)
     if (!k_ranks[r].data || !v_ranks[r].data) return SBDA_ERR_INVALID;
   // One shard is the whole sequence: the unsharded kernels (windowed where they apply).
-  if (world == 1) return sbda_b200_forward(dtype, shape, offsets, n_offsets, scale, q, k_ranks[0], v_ranks[0], out, lse, stream);
+  if (world == 1)
+    return sbda_b200_forward_ex(family, dtype, shape, offsets, n_offsets, scale, q, k_ranks[0], v_ranks[0], out, lse,
+                                stream);
   const int e = elem_size(dtype);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   {  // The windowed kernels, when they serve the schedule and every view suits the copy engine.
     V2Plan p2;
-    if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, Ls, D, e, H / Hkv, B, H, &p2, world * Ls) &&
+    if (family == kFamilyAuto && plan_v2(offsets, n_offsets, Ls, D, e, H / Hkv, B, H, &p2, world * Ls) &&
         Ls % p2.tile == 0 && vector_ok(q, B, H, Ls, D, e) && vector_ok(out, B, H, Ls, D, e)) {
       FwdV2Params p;
       memset(&p, 0, sizeof(p));
@@ -861,12 +878,13 @@ extern "C" int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int3
   return v1_forward_sharded(dtype, maps, p, pl, reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int32_t* offsets,
-                                          int32_t n_offsets, float scale, int32_t rank, int32_t world,
-                                          const sbda_tensor* q_ranks, const sbda_tensor* k_ranks,
-                                          const sbda_tensor* v_ranks, const sbda_tensor* grad_out_ranks,
-                                          const float* const* lse_ranks, sbda_tensor grad_q, sbda_tensor grad_k,
-                                          sbda_tensor grad_v, void* stream) {
+extern "C" int sbda_b200_backward_sharded_ex(int family, int dtype, sbda_shape shape, const int32_t* offsets,
+                                             int32_t n_offsets, float scale, int32_t rank, int32_t world,
+                                             const sbda_tensor* q_ranks, const sbda_tensor* k_ranks,
+                                             const sbda_tensor* v_ranks, const sbda_tensor* grad_out_ranks,
+                                             const float* const* lse_ranks, sbda_tensor grad_q, sbda_tensor grad_k,
+                                             sbda_tensor grad_v, void* stream) {
+  if (!family_ok(family)) return SBDA_ERR_INVALID;
   int st = validate(dtype, shape, offsets, n_offsets);
   if (st != SBDA_OK) return st;
   if (world < 1 || world > kMaxShards || rank < 0 || rank >= world || !q_ranks || !k_ranks || !v_ranks ||
@@ -879,12 +897,12 @@ extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int
     if (!q_ranks[r].data || !k_ranks[r].data || !v_ranks[r].data || !grad_out_ranks[r].data || !lse_ranks[r])
       return SBDA_ERR_INVALID;
   if (world == 1)
-    return sbda_b200_backward(dtype, shape, offsets, n_offsets, scale, q_ranks[0], k_ranks[0], v_ranks[0],
-                              grad_out_ranks[0], lse_ranks[0], grad_q, grad_k, grad_v, stream);
+    return sbda_b200_backward_ex(family, dtype, shape, offsets, n_offsets, scale, q_ranks[0], k_ranks[0],
+                                 v_ranks[0], grad_out_ranks[0], lse_ranks[0], grad_q, grad_k, grad_v, stream);
   const int e = elem_size(dtype);
   {  // The windowed kernels, when they serve the schedule and every view suits the copy engine.
     V2Plan p2;
-    if (g_kernel_path.load() == 0 && plan_v2(offsets, n_offsets, Ls, D, e, H / Hkv, B, H, &p2, world * Ls) &&
+    if (family == kFamilyAuto && plan_v2(offsets, n_offsets, Ls, D, e, H / Hkv, B, H, &p2, world * Ls) &&
         Ls % p2.tile == 0 && vector_ok(grad_q, B, H, Ls, D, e) && vector_ok(grad_k, B, H, Ls, D, e) &&
         vector_ok(grad_v, B, H, Ls, D, e)) {
       BwdV2Params p;
@@ -972,4 +990,22 @@ extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int
          encode_ranks(maps.vH, nullptr, v_ranks, world, dtype, B, Hkv, Ls, D, pl.pitch, pl.g.Hn);
   if (!ok) return SBDA_ERR_UNSUPPORTED;
   return v1_backward_sharded(dtype, maps, p, pl, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbda_b200_forward_sharded(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                         float scale, int32_t rank, int32_t world, sbda_tensor q,
+                                         const sbda_tensor* k_ranks, const sbda_tensor* v_ranks, sbda_tensor out,
+                                         float* lse, void* stream) {
+  return sbda_b200_forward_sharded_ex(kFamilyAuto, dtype, shape, offsets, n_offsets, scale, rank, world, q, k_ranks,
+                                      v_ranks, out, lse, stream);
+}
+
+extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int32_t* offsets,
+                                          int32_t n_offsets, float scale, int32_t rank, int32_t world,
+                                          const sbda_tensor* q_ranks, const sbda_tensor* k_ranks,
+                                          const sbda_tensor* v_ranks, const sbda_tensor* grad_out_ranks,
+                                          const float* const* lse_ranks, sbda_tensor grad_q, sbda_tensor grad_k,
+                                          sbda_tensor grad_v, void* stream) {
+  return sbda_b200_backward_sharded_ex(kFamilyAuto, dtype, shape, offsets, n_offsets, scale, rank, world, q_ranks,
+                                       k_ranks, v_ranks, grad_out_ranks, lse_ranks, grad_q, grad_k, grad_v, stream);
 }

@@ -19,12 +19,20 @@ version, since the kernel geometry is planned on the host.
 
 The lower-level ``sbda_forward`` / ``sbda_backward`` expose the C ABI
 directly (no autograd) and return / take the fp32 log-sum-exp.
+
+``kernel_family("general")`` (a context manager) pins the kernel family of the
+calls made inside it, for tests and benchmarks that compare families.  It is
+context-local (``contextvars``): other threads keep the automatic choice, and
+the autograd op records the family at forward time so its backward, which
+runs on autograd's worker thread, uses the same family.
 """
 
 from __future__ import annotations
 
+import contextlib
+import contextvars
 import threading
-from typing import Sequence
+from typing import Iterator, Sequence
 
 import torch
 from torch import Tensor
@@ -36,6 +44,25 @@ _DTYPES = {
     torch.float16: _lib.SBDA_DTYPE_F16,
     torch.bfloat16: _lib.SBDA_DTYPE_BF16,
 }
+
+_family: contextvars.ContextVar[int] = contextvars.ContextVar("sbda_b200_kernel_family", default=0)
+
+
+@contextlib.contextmanager
+def kernel_family(family: str | int) -> Iterator[int]:
+    """Pin the kernel family (``"auto"``, ``"general"``, ``"uniform"``) of the SBDA calls made
+    in this context; yields the family code."""
+    token = _family.set(_lib.family_code(family))
+    try:
+        yield _family.get()
+    finally:
+        _family.reset(token)
+
+
+def current_family() -> int:
+    """Family code of this context (0 = automatic)."""
+    return _family.get()
+
 
 _offset_cache: dict[int, tuple[object, int, tuple[int, ...]]] = {}
 _offset_lock = threading.Lock()
@@ -105,12 +132,15 @@ def _check_source_mask(mask: Tensor, q: Tensor) -> None:
 
 def sbda_forward(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int], *,
                  scale: float | None = None, out: Tensor | None = None,
-                 lse: Tensor | None = None, source_mask: Tensor | None = None) -> tuple[Tensor, Tensor]:
+                 lse: Tensor | None = None, source_mask: Tensor | None = None,
+                 family: int | None = None) -> tuple[Tensor, Tensor]:
     """Forward through the C ABI: returns ``(out, lse)``; ``lse`` is fp32 ``[B,H,L]``.
 
     ``source_mask`` (optional, uint8 ``[B, L]``): bit s of row i allows source s of that row
-    (``sbda_b200_forward_masked``).
+    (``sbda_b200_forward_masked``).  ``family``: kernel family code (default: this context's,
+    see :func:`kernel_family`).
     """
+    family = current_family() if family is None else _lib.family_code(family)
     offsets = tuple(int(o) for o in offsets)
     batch, heads, length, head_dim = q.shape
     if out is None:
@@ -123,8 +153,8 @@ def sbda_forward(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int], *,
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         if source_mask is None:
-            status = lib.sbda_b200_forward(
-                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+            status = lib.sbda_b200_forward_ex(
+                family, _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
                 _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(out), lse.data_ptr(), stream,
             )
         else:
@@ -141,9 +171,10 @@ def sbda_forward(q: Tensor, k: Tensor, v: Tensor, offsets: Sequence[int], *,
 def sbda_backward(q: Tensor, k: Tensor, v: Tensor, grad_out: Tensor, lse: Tensor,
                   offsets: Sequence[int], *, scale: float | None = None,
                   grads: tuple[Tensor, Tensor, Tensor] | None = None,
-                  source_mask: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
-    """Backward through the C ABI: returns ``(dq, dk, dv)`` in the input dtype (``source_mask`` as
-    in :func:`sbda_forward`)."""
+                  source_mask: Tensor | None = None, family: int | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    """Backward through the C ABI: returns ``(dq, dk, dv)`` in the input dtype (``source_mask`` and
+    ``family`` as in :func:`sbda_forward`)."""
+    family = current_family() if family is None else _lib.family_code(family)
     offsets = tuple(int(o) for o in offsets)
     if grad_out.dtype != q.dtype:
         grad_out = grad_out.to(q.dtype)
@@ -160,8 +191,8 @@ def sbda_backward(q: Tensor, k: Tensor, v: Tensor, grad_out: Tensor, lse: Tensor
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         if source_mask is None:
-            status = lib.sbda_b200_backward(
-                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+            status = lib.sbda_b200_backward_ex(
+                family, _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
                 _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(grad_out), lse.data_ptr(),
                 _tensor_arg(dq), _tensor_arg(dk), _tensor_arg(dv), stream,
             )
@@ -187,7 +218,8 @@ class _SBDAFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q: Tensor, k: Tensor, v: Tensor, offsets: tuple[int, ...],
                 source_mask: Tensor | None = None) -> Tensor:
-        out, lse = sbda_forward(q, k, v, offsets, source_mask=source_mask)
+        ctx.family = current_family()
+        out, lse = sbda_forward(q, k, v, offsets, source_mask=source_mask, family=ctx.family)
         ctx.save_for_backward(q, k, v, lse)
         ctx.offsets = offsets
         ctx.source_mask = source_mask
@@ -196,7 +228,8 @@ class _SBDAFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out: Tensor):
         q, k, v, lse = ctx.saved_tensors
-        dq, dk, dv = sbda_backward(q, k, v, grad_out, lse, ctx.offsets, source_mask=ctx.source_mask)
+        dq, dk, dv = sbda_backward(q, k, v, grad_out, lse, ctx.offsets, source_mask=ctx.source_mask,
+                                   family=ctx.family)
         return dq, dk, dv, None, None
 
 
@@ -323,7 +356,7 @@ def device_status(reset: bool = True) -> int:
 
 
 __all__ = [
-    "fused_sbda", "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_key_backward",
+    "current_family", "kernel_family", "fused_sbda", "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_key_backward",
     "fused_sbda_gqa_key_backward", "sbda_attention", "sbda_forward", "sbda_backward", "host_offsets",
     "device_status",
 ]

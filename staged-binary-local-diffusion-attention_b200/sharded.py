@@ -1,7 +1,8 @@
 """SBDA attention over contiguous sequence shards on several GPUs.
 
 Rank ``r`` of a process group holds positions ``[r * L, (r + 1) * L)`` of one sequence (the
-reference runs one sequence on one GPU; long sequences are its scaling axis, SURVEY config 5).
+reference runs one sequence on one GPU; a single sequence of millions of positions is the case
+this module scales).
 A query's dyadic source ``i - d`` and a key's dyadic consumer ``j + d`` may live on another
 rank: the kernels (the windowed ones for SBDA schedules, the general ones otherwise) stage those
 rows per tile straight from the owning GPU's buffer over NVLink (non-multicast TMA loads of peer
@@ -23,7 +24,7 @@ import torch.distributed as dist
 from torch import Tensor
 
 from . import _lib
-from .ops import _DTYPES, _tensor_arg, host_offsets
+from .ops import _DTYPES, _tensor_arg, current_family, host_offsets
 
 
 def shard_bounds(total_len: int, world: int, rank: int) -> tuple[int, int]:
@@ -110,22 +111,27 @@ def sharded_forward(q: Tensor, k: Tensor, v: Tensor, offsets: Tensor | Sequence[
                     *, out: Tensor | None = None, lse: Tensor | None = None) -> tuple[Tensor, Tensor]:
     """This rank's output rows and fp32 LSE ``[B,H,L]`` for its shard.
 
-    ``q, k, v``: this rank's shard as ``[B, H, L, D]`` views; ``k``, ``v`` (and ``lse`` if given)
-    must come from ``shards.empty``.  Issues a device-side barrier first so every rank's K/V
-    are complete; the caller barriers again before overwriting K/V.
+    ``q, k, v``: this rank's shard as ``[B, H, L, D]`` views; ``k``, ``v`` and ``lse`` must come
+    from ``shards.empty`` (the backward reads every rank's LSE).  ``lse`` is required: a
+    symmetric allocation is a collective, so the caller makes one per layer up front (for
+    example with ``shards.empty(B, H, L, dtype=torch.float32)``) and reuses it every step.
+    Issues a device-side barrier first so every rank's K/V are complete; the caller barriers
+    again before overwriting K/V.
     """
+    if lse is None:
+        raise ValueError("sharded_forward needs a preallocated symmetric lse buffer (shards.empty)")
     values = host_offsets(offsets)
     batch, heads, length, head_dim = q.shape
     if out is None:
         out = torch.empty_like(q)
-    if lse is None:
-        lse = shards.empty(batch, heads, length, dtype=torch.float32, device=q.device)
+    if lse.shape != (batch, heads, length) or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise ValueError("lse must be a contiguous fp32 [B, H, L] tensor")
     shards.barrier()
     lib = _lib.load()
     shape = _lib.SbdaShape(batch, heads, k.shape[1], length, head_dim)
     with torch.cuda.device(q.device):
-        status = lib.sbda_b200_forward_sharded(
-            _DTYPES[q.dtype], shape, _lib.offsets_array(values), len(values), head_dim ** -0.5,
+        status = lib.sbda_b200_forward_sharded_ex(
+            current_family(), _DTYPES[q.dtype], shape, _lib.offsets_array(values), len(values), head_dim ** -0.5,
             shards.rank, shards.world, _tensor_arg(q), _rank_args(shards, k), _rank_args(shards, v),
             _tensor_arg(out), lse.data_ptr(), torch.cuda.current_stream(q.device).cuda_stream)
     _lib.raise_for_status(status, "sbda_b200_forward_sharded")
@@ -143,8 +149,8 @@ def sharded_backward(q: Tensor, k: Tensor, v: Tensor, grad_out: Tensor, lse: Ten
     shape = _lib.SbdaShape(batch, heads, k.shape[1], length, head_dim)
     lse_ptrs = (ctypes.c_void_p * shards.world)(*shards.peer_pointers(lse))
     with torch.cuda.device(q.device):
-        status = lib.sbda_b200_backward_sharded(
-            _DTYPES[q.dtype], shape, _lib.offsets_array(values), len(values), head_dim ** -0.5,
+        status = lib.sbda_b200_backward_sharded_ex(
+            current_family(), _DTYPES[q.dtype], shape, _lib.offsets_array(values), len(values), head_dim ** -0.5,
             shards.rank, shards.world, _rank_args(shards, q), _rank_args(shards, k), _rank_args(shards, v),
             _rank_args(shards, grad_out), lse_ptrs, _tensor_arg(dq), _tensor_arg(dk), _tensor_arg(dv),
             torch.cuda.current_stream(q.device).cuda_stream)

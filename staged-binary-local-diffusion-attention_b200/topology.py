@@ -94,8 +94,12 @@ _RULES: dict[str, Callable[[int, int, int], tuple[int, ...]]] = {
 }
 
 
-def topology_offsets(layer: int, *, topology: str = "sbda", total_layers: int = 12) -> tuple[int, ...]:
-    """Exact left offsets of one layer (``topology.py:24-155``)."""
+def topology_offsets(layer: int, *, topology: str = "binary", total_layers: int = 12) -> tuple[int, ...]:
+    """Exact left offsets of one layer (``topology.py:24-155``).
+
+    The default topology is ``"binary"``, as in the reference (``topology.py:24-28``); SBDA
+    stacks pass ``topology="sbda"`` (or use :func:`sbda_layer_offsets`).
+    """
     if layer < 1:
         raise ValueError("layer must be positive")
     if total_layers < 1:

@@ -42,11 +42,21 @@ def test_abi_version_matches_header(lib):
     assert lib.sbda_b200_abi_version() == version
 
 
-def test_kernel_path_switch(lib):
-    assert _lib.set_kernel_path(1) == 0
-    assert _lib.set_kernel_path(0) == 1
-    with pytest.raises(ValueError):
-        _lib.set_kernel_path(7)
+def test_kernel_family_is_an_argument(lib):
+    """The family is a per-call argument: unknown families are rejected before any device work,
+    and the library exports no process-wide switch."""
+    assert not hasattr(lib, "sbda_b200_set_kernel_path")
+    t = _lib.SbdaTensor(16, 1 << 20, 1 << 14, 64, 1)
+    s = _lib.SbdaShape(1, 2, 2, 64, 64)
+    offs = _lib.offsets_array((0, 1, 2, 4))
+    for bad in (-1, 3, 7):
+        assert lib.sbda_b200_forward_ex(bad, 2, s, offs, 4, 0.1, t, t, t, t, 16, None) == _lib.SBDA_ERR_INVALID
+        assert lib.sbda_b200_backward_ex(bad, 2, s, offs, 4, 0.1, t, t, t, t, 16, t, t, t, None) \
+            == _lib.SBDA_ERR_INVALID
+    # Valid families on an empty problem: a successful no-op.
+    empty = _lib.SbdaShape(0, 2, 2, 64, 64)
+    for family in (0, 1, 2):
+        assert lib.sbda_b200_forward_ex(family, 2, empty, offs, 4, 0.1, t, t, t, t, 16, None) == _lib.SBDA_OK
 
 
 def test_status_strings(lib):
@@ -80,12 +90,26 @@ def test_forward_validation_codes(lib):
     assert _call_forward(lib, shape=(1, 2, 2, 0, 64)) == _lib.SBDA_OK
 
 
-def test_kernel_path_values(lib):
-    assert _lib.set_kernel_path(2) == 0
-    assert _lib.set_kernel_path(1) == 2
-    assert _lib.set_kernel_path(0) == 1
+def test_kernel_family_context_is_local():
+    """``kernel_family`` pins the family in this context only; another thread sees ``auto``."""
+    import threading
+
+    import sbda_b200
+
+    assert sbda_b200.current_family() == 0
+    seen = []
+    with sbda_b200.kernel_family("uniform") as code:
+        assert code == 2 and sbda_b200.current_family() == 2
+        worker = threading.Thread(target=lambda: seen.append(sbda_b200.current_family()))
+        worker.start()
+        worker.join()
+        with sbda_b200.kernel_family("general"):
+            assert sbda_b200.current_family() == 1
+        assert sbda_b200.current_family() == 2
+    assert sbda_b200.current_family() == 0 and seen == [0]
     with pytest.raises(ValueError):
-        _lib.set_kernel_path(3)
+        with sbda_b200.kernel_family("fast"):
+            pass
 
 
 def test_backward_validation_codes(lib):

@@ -23,9 +23,8 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture(params=["auto", "general", "uniform"])
 def kernel_path(request):
     """Runs a test through the windowed kernels (auto), the general ones and the uniform ones."""
-    previous = _lib.set_kernel_path({"auto": 0, "general": 1, "uniform": 2}[request.param])
-    yield request.param
-    _lib.set_kernel_path(previous)
+    with sbda_b200.kernel_family(request.param):
+        yield request.param
 
 TOL = {torch.float32: dict(rtol=1e-5, atol=1e-5),
        torch.bfloat16: dict(rtol=0.0, atol=2e-2),
@@ -137,27 +136,27 @@ def test_reference_golden_vectors(golden):
 @pytest.mark.parametrize("layer", list(range(1, 13)))
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_every_layer_schedule(layer, dtype, kernel_path):
-    offsets = sbda_b200.topology_offsets(layer)
+    offsets = sbda_b200.topology_offsets(layer, topology="sbda")
     _check(2, 2, 1000, 64, dtype, offsets, seed=layer)
 
 
 @pytest.mark.parametrize("length", [1, 2, 3, 7, 63, 64, 65, 129, 4099, 20000])
 def test_ragged_lengths(length, kernel_path):
     for layer in (1, 3, 8, 13):
-        _check(1, 3, length, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), seed=length + layer)
+        _check(1, 3, length, 64, torch.bfloat16, sbda_b200.topology_offsets(layer, topology="sbda"), seed=length + layer)
 
 
 @pytest.mark.parametrize("dim", [8, 16, 24, 40, 64, 96, 128])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_head_dims_and_dtypes(dim, dtype, kernel_path):
     for layer in (3, 9):
-        _check(1, 2, 300, dim, dtype, sbda_b200.topology_offsets(layer), seed=dim)
+        _check(1, 2, 300, dim, dtype, sbda_b200.topology_offsets(layer, topology="sbda"), seed=dim)
 
 
 @pytest.mark.parametrize("layout", ["bhld", "blhd", "misaligned"])
 def test_layouts(layout, kernel_path):
     for layer in (2, 7, 10):
-        _check(2, 2, 700, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), layout=layout)
+        _check(2, 2, 700, 64, torch.bfloat16, sbda_b200.topology_offsets(layer, topology="sbda"), layout=layout)
     _check(1, 2, 200, 6, torch.float32, (0, 1, 2, 16), layout="bhld")  # 12-byte rows: generic path
 
 
@@ -170,8 +169,8 @@ def test_gqa_reference_protocol():
 @pytest.mark.parametrize("kv_heads", [1, 2, 4])
 def test_gqa_groups(kv_heads):
     for layer in (4, 11):
-        _check(2, 8, 500, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), kv_heads=kv_heads)
-        _check(1, 8, 257, 32, torch.float32, sbda_b200.topology_offsets(layer), kv_heads=kv_heads)
+        _check(2, 8, 500, 64, torch.bfloat16, sbda_b200.topology_offsets(layer, topology="sbda"), kv_heads=kv_heads)
+        _check(1, 8, 257, 32, torch.float32, sbda_b200.topology_offsets(layer, topology="sbda"), kv_heads=kv_heads)
 
 
 def test_other_offset_sets(kernel_path):
@@ -184,23 +183,37 @@ def test_other_offset_sets(kernel_path):
 @pytest.mark.parametrize("layer", [1, 2, 3, 6, 7, 8, 12, 15])
 def test_chain_walk_segments(layer, kernel_path):
     """Long sequences split the backward's chain walks into segments with a carry-only first tile."""
-    _check(1, 4, 65536, 64, torch.bfloat16, sbda_b200.topology_offsets(layer), seed=100 + layer)
+    _check(1, 4, 65536, 64, torch.bfloat16, sbda_b200.topology_offsets(layer, topology="sbda"), seed=100 + layer)
 
 
 def test_kernel_families_agree():
     """The windowed and the general kernels give the same results on the same inputs."""
     q, k, v, do = _inputs(2, 4, 3000, 64, torch.bfloat16, seed=11)
     for layer in (2, 5, 7, 9, 11):
-        offsets = sbda_b200.topology_offsets(layer)
-        previous = _lib.set_kernel_path(0)
-        try:
+        offsets = sbda_b200.topology_offsets(layer, topology="sbda")
+        with sbda_b200.kernel_family("auto"):
             auto = _run(q, k, v, do, offsets)
-            _lib.set_kernel_path(1)
+        with sbda_b200.kernel_family("general"):
             general = _run(q, k, v, do, offsets)
-        finally:
-            _lib.set_kernel_path(previous)
         for a, b in zip(auto, general):
             torch.testing.assert_close(a.float(), b.float(), rtol=0, atol=1.6e-2)
+
+
+def test_backward_uses_the_forwards_family():
+    """The autograd op records the kernel family at forward time: a backward run after the
+    context has changed (or on autograd's worker thread) still uses the forward's family."""
+    q, k, v, do = _inputs(1, 4, 3000, 64, torch.bfloat16, seed=12)
+    offsets = sbda_b200.topology_offsets(9, topology="sbda")
+    ref = {}
+    for family in ("auto", "general"):
+        with sbda_b200.kernel_family(family):
+            ref[family] = _run(q, k, v, do, offsets)
+    qs, ks, vs = (t.detach().requires_grad_() for t in (q, k, v))
+    with sbda_b200.kernel_family("general"):
+        out = sbda_b200.fused_sbda_key_backward(qs, ks, vs, offsets)
+    out.backward(do)  # outside the context: still the general family
+    for a, b in zip((out, qs.grad, ks.grad, vs.grad), ref["general"]):
+        assert torch.equal(a, b)
 
 
 def test_offsets_without_self_source(kernel_path):
@@ -210,8 +223,8 @@ def test_offsets_without_self_source(kernel_path):
 
 def test_deterministic(kernel_path):
     q, k, v, do = _inputs(2, 4, 5000, 64, torch.bfloat16, seed=9)
-    first = _run(q, k, v, do, sbda_b200.topology_offsets(9))
-    second = _run(q, k, v, do, sbda_b200.topology_offsets(9))
+    first = _run(q, k, v, do, sbda_b200.topology_offsets(9, topology="sbda"))
+    second = _run(q, k, v, do, sbda_b200.topology_offsets(9, topology="sbda"))
     for a, b in zip(first, second):
         assert torch.equal(a, b)
 
@@ -219,7 +232,7 @@ def test_deterministic(kernel_path):
 def test_full_size_sampled_rows(kernel_path):
     """1M positions at layer 20 (dyadic 2^19): sampled rows against the fp64 row oracle."""
     length = 1 << 20
-    offsets = sbda_b200.topology_offsets(20)
+    offsets = sbda_b200.topology_offsets(20, topology="sbda")
     q, k, v, do = _inputs(1, 4, length, 64, torch.bfloat16, seed=20)
     out, dq, dk, dv = _run(q, k, v, do, offsets)
     g = torch.Generator().manual_seed(1)
@@ -260,7 +273,7 @@ def test_module_matches_reference_golden(golden):
 def test_config2_full_parity():
     """Config 2: B 4, 8 heads x 64, L 32768, layer 10 (offsets 0, 1, 2, 512), bf16, vs the fp32 oracle."""
     q, k, v, do = _inputs(4, 8, 32768, 64, torch.bfloat16, seed=2)
-    offsets = sbda_b200.topology_offsets(10)
+    offsets = sbda_b200.topology_offsets(10, topology="sbda")
     out, dq, dk, dv = _run(q, k, v, do, offsets)
     ro, rdq, rdk, rdv = orc.exact_attention_grads(q, k, v, offsets, do)
     for name, got, ref in (("O", out, ro), ("dQ", dq, rdq), ("dK", dk, rdk), ("dV", dv, rdv)):
@@ -279,7 +292,7 @@ def test_config3_stack_sampled_rows():
     batches = torch.tensor([0, 7])
     dev_rows, dev_batches = rows.cuda(), batches.cuda()
     for layer in range(1, 16):
-        offsets = sbda_b200.topology_offsets(layer, total_layers=15)
+        offsets = sbda_b200.topology_offsets(layer, topology="sbda", total_layers=15)
         q, k, v, do = _inputs(8, 8, 32768, 64, torch.bfloat16, seed=300 + layer)
         out, dq, dk, dv = _run(q, k, v, do, offsets)
         qc, kc, vc, doc = (t.detach()[dev_batches].cpu() for t in (q, k, v, do))
@@ -347,7 +360,7 @@ def test_source_masks_match_oracle(dtype):
     sbda_b200_backward_masked against the oracle's masked route (left_v2.py:349-396)."""
     g = torch.Generator().manual_seed(5)
     for layer, length, kv_heads in ((3, 300, 4), (7, 700, 4), (10, 1500, 2), (2, 130, 4)):
-        offsets = sbda_b200.topology_offsets(layer)
+        offsets = sbda_b200.topology_offsets(layer, topology="sbda")
         q, k, v, do = _inputs(2, 4, length, 64, dtype, kv_heads=kv_heads, seed=layer)
         valid_mask = torch.rand(2, length, generator=g) > 0.1
         valid_mask[1, length - 17:] = False

@@ -132,6 +132,23 @@ def test_every_topology_matches_reference_table():
     assert checked > 1900  # 31 topologies x 22 layers x 3 stack depths, less the capped h3 rows
 
 
+def test_topology_default_is_the_references():
+    """With no ``topology=`` the drop-in returns the reference's default schedule, ``binary``
+    (``BiAttn/topology.py:24-28``), for every layer and stack depth the reference table holds."""
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(__file__), "golden", "topology_table.json")) as handle:
+        table = json.load(handle)
+    assert sbda_b200.topology_offsets(5) == (0, 16)
+    assert sbda_b200.topology_offsets(1) == (0, 1)
+    for total, rows in table["offsets"]["binary"].items():
+        for layer, expected in zip(table["layers"], rows):
+            assert list(sbda_b200.topology_offsets(layer, total_layers=int(total))) == expected, (total, layer)
+            if int(total) == 12:
+                assert list(sbda_b200.topology_offsets(layer)) == expected, layer
+
+
 def test_path_golden_offsets_match_topologies(path_golden):
     for case in path_golden.cases:
         assert list(sbda_b200.topology_offsets(case["layer"], topology=case["topology"], total_layers=12)) \

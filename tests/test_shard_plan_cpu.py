@@ -95,3 +95,15 @@ def test_shard_link_model_counts_remote_rows():
             target += bound
         assert model["max_remote_bytes_one_layer"] == worst
         assert abs(model["target_ms"] - target * 1e-6) < 1e-9 * target
+
+
+def test_sharded_forward_needs_a_preallocated_lse():
+    """``sharded_forward`` never allocates symmetric memory itself (an allocation there would be a
+    collective and a buffer the group keeps): without ``lse`` it raises before any work."""
+    import pytest
+
+    from sbda_b200.sharded import sharded_forward
+
+    q = torch.zeros(1, 2, 64, 16)
+    with pytest.raises(ValueError, match="lse"):
+        sharded_forward(q, q, q, (0, 1), shards=None)

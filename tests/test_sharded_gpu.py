@@ -44,29 +44,27 @@ def _emulated(q, k, v, do, offsets, world):
     stream = torch.cuda.current_stream().cuda_stream
     ks, vs = _arr([sl(k, r) for r in range(world)]), _arr([sl(v, r) for r in range(world)])
     for r in range(world):
-        st = lib.sbda_b200_forward_sharded(_DTYPES[q.dtype], shape, offs, len(offsets), dim ** -0.5, r, world,
-                                           _tensor_arg(sl(q, r)), ks, vs, _tensor_arg(sl(out, r)),
-                                           lse[r].data_ptr(), stream)
+        st = lib.sbda_b200_forward_sharded_ex(sbda_b200.current_family(), _DTYPES[q.dtype], shape, offs,
+                                              len(offsets), dim ** -0.5, r, world, _tensor_arg(sl(q, r)), ks, vs,
+                                              _tensor_arg(sl(out, r)), lse[r].data_ptr(), stream)
         assert st == 0, _lib.status_string(st)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     qs, dos = _arr([sl(q, r) for r in range(world)]), _arr([sl(do, r) for r in range(world)])
     lses = (ctypes.c_void_p * world)(*[lse[r].data_ptr() for r in range(world)])
     for r in range(world):
-        st = lib.sbda_b200_backward_sharded(_DTYPES[q.dtype], shape, offs, len(offsets), dim ** -0.5, r, world,
-                                            qs, ks, vs, dos, lses, _tensor_arg(sl(dq, r)), _tensor_arg(sl(dk, r)),
-                                            _tensor_arg(sl(dv, r)), stream)
+        st = lib.sbda_b200_backward_sharded_ex(sbda_b200.current_family(), _DTYPES[q.dtype], shape, offs,
+                                               len(offsets), dim ** -0.5, r, world, qs, ks, vs, dos, lses,
+                                               _tensor_arg(sl(dq, r)), _tensor_arg(sl(dk, r)),
+                                               _tensor_arg(sl(dv, r)), stream)
         assert st == 0, _lib.status_string(st)
     return out, dq, dk, dv
 
 
 def _whole(q, k, v, do, offsets, path=1):
     """The unsharded kernels of family ``path`` (0 = auto, 1 = general) on the whole sequence."""
-    previous = _lib.set_kernel_path(path)
-    try:
+    with sbda_b200.kernel_family(path):
         out, lse = sbda_b200.sbda_forward(q, k, v, offsets)
         dq, dk, dv = sbda_b200.sbda_backward(q, k, v, do, lse, offsets)
-    finally:
-        _lib.set_kernel_path(previous)
     return out, dq, dk, dv
 
 
@@ -81,16 +79,13 @@ def test_emulated_shards_match_whole_sequence(world, path):
     g = torch.Generator(device="cuda").manual_seed(world)
     make = lambda h: torch.randn(1, total, h, 64, device="cuda", generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)  # noqa: E731
     q, k, v, do = make(4), make(4), make(4), make(4)
-    previous = _lib.set_kernel_path(path)
-    try:
+    with sbda_b200.kernel_family(path):
         for layer in (1, 2, 3, 5, 6, 7, 8, 10, 11, 12, 13, 14):
-            offsets = sbda_b200.topology_offsets(layer)
+            offsets = sbda_b200.topology_offsets(layer, topology="sbda")
             got = _emulated(q, k, v, do, offsets, world)
             ref = _whole(q, k, v, do, offsets, path)
             for name, a, b in zip(("O", "dQ", "dK", "dV"), got, ref):
                 assert torch.equal(a, b), f"layer {layer} world {world}: {name} differs"
-    finally:
-        _lib.set_kernel_path(previous)
     assert sbda_b200.device_status(reset=True) == 0
 
 
@@ -135,10 +130,11 @@ def _two_rank_worker(rank: int, world: int, port: int, result: "torch.multiproce
         for buf, src in zip(bufs, full):
             buf.copy_(src[:, lo:hi])
         q, k, v, do = (b.permute(0, 2, 1, 3) for b in bufs)
+        lse = shards.empty(1, 4, hi - lo, dtype=torch.float32, device=dev)
         ok = True
         for layer in (3, 9, 12, 13, 14):
-            offsets = sbda_b200.topology_offsets(layer)
-            out, lse = sharded_forward(q, k, v, offsets, shards)
+            offsets = sbda_b200.topology_offsets(layer, topology="sbda")
+            out, _ = sharded_forward(q, k, v, offsets, shards, lse=lse)
             dq, dk, dv = sharded_backward(q, k, v, do, lse, offsets, shards)
             shards.barrier()
             whole = [t.permute(0, 2, 1, 3) for t in full]
@@ -170,3 +166,28 @@ def test_two_gpu_shards_over_nvlink():
     for rank, ok, fault in outcomes:
         assert ok, f"rank {rank} differs from the single-GPU result"
         assert fault == 0
+
+
+def test_repeated_sharded_calls_keep_state_flat():
+    """A hundred sharded forward + backward calls on a one-rank group hold no new buffers or
+    handles: ``lse`` is the caller's, and nothing is registered per call."""
+    from sbda_b200.sharded import ShardGroup, sharded_backward, sharded_forward
+
+    shards = ShardGroup()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v, do = (torch.randn(1, 4096, 4, 64, device="cuda", generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)
+                   for _ in range(4))
+    lse = shards.empty(1, 4, 4096, dtype=torch.float32)
+    out = torch.empty_like(q)
+    offsets = sbda_b200.topology_offsets(9, topology="sbda")
+    sharded_forward(q, k, v, offsets, shards, out=out, lse=lse)
+    sharded_backward(q, k, v, do, lse, offsets, shards)
+    torch.cuda.synchronize()
+    handles, allocated = len(shards._handles), torch.cuda.memory_allocated()
+    for _ in range(100):
+        sharded_forward(q, k, v, offsets, shards, out=out, lse=lse)
+        grads = sharded_backward(q, k, v, do, lse, offsets, shards)
+        del grads
+    torch.cuda.synchronize()
+    assert len(shards._handles) == handles
+    assert torch.cuda.memory_allocated() == allocated
