@@ -12,8 +12,13 @@ step time.  Each tensor is 512 MiB (> 126 MB L2), so no L2 flush is needed.
 Under torchrun each rank runs an independent sequence (batch sharding, no
 data-path collective; weak scaling); the timed region is bracketed by a
 barrier and synchronize on every rank and the slowest rank's time is used.
-``--impl reference`` times the reference's algorithm (the CPU oracle port of
-``BiAttn/left_v2.py``'s exact path) on the host cores instead.
+The same JSON line carries the other configurations as blocks: ``cfg2`` (one
+layer at B 4 x 8 heads x 32,768, one GPU), ``cfg3_batch_head`` (15 layers at
+B 8 x 8 heads x 32,768 with the (batch, head) sequences split across the
+ranks: strong scaling) and ``cfg5_seqshard`` (one 4,194,304-position sequence
+x 22 layers in contiguous shards across the ranks, halos over NVLink: strong
+scaling).  ``--impl reference`` times the reference's algorithm (the CPU
+oracle port of ``BiAttn/left_v2.py``'s exact path) on the host cores instead.
 """
 
 from __future__ import annotations
@@ -59,6 +64,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-blocks", action="store_true",
+                   help="skip the config-2, config-3 and config-5 blocks of the default line")
     p.add_argument("--cpu-sample-length", type=int, default=CPU_SAMPLE_POSITIONS)
     return p.parse_args()
 
@@ -87,17 +94,18 @@ def measured_peak_gbs() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic() -> float | None:
-    """Per-launch DRAM bytes of the backward kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "sbda_bwd_kernel_cfg4.md")
-    try:
-        with open(path) as handle:
-            for line in handle:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+# DRAM bytes per (batch, head, position) row of one windowed backward launch (dram__bytes_read.sum
+# + dram__bytes_write.sum), measured by ncu on a small case of the same kernel: 262,144 positions
+# x 4 heads x 64, bf16, layers 4, 10 and 19 (local, chain and long-chain walks), averaged over the
+# three launches.  Traffic grows in proportion to the rows, so a full launch's traffic is this
+# figure times its rows.  The capture command and its figures are in
+# profiles/sbda_bwd_kernel_small_case.md.  None until measured.
+BWD_DRAM_BYTES_PER_ROW: float | None = None
+
+
+def backward_traffic(rows: int) -> float | None:
+    """Per-launch DRAM traffic of the windowed backward for ``rows`` rows (see above)."""
+    return None if BWD_DRAM_BYTES_PER_ROW is None else BWD_DRAM_BYTES_PER_ROW * rows
 
 
 def shard_link_model(total: int, world: int, heads: int, head_dim: int, elem: int, offsets_per_layer,
@@ -258,6 +266,7 @@ def run_b200(args) -> None:
     if world > 1:
         import datetime
 
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     def barrier():
@@ -353,7 +362,7 @@ def run_b200(args) -> None:
     value = positions / (step_ms * 1e-3) / 1e6
     dominant = ("sbda_bwd_kernel", bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else ("sbda_fwd_kernel", fwd_bytes, fwd_ms)
     achieved = dominant[1] / (dominant[2] * 1e-3) / 1e9
-    traffic = profiled_traffic() if dominant[0] == "sbda_bwd_kernel" else None
+    traffic = backward_traffic(rows) if dominant[0] == "sbda_bwd_kernel" else None
     step_bytes = layers * (fwd_bytes + bwd_bytes)
     step_gbs = step_bytes / (step_ms * 1e-3) / 1e9
 
@@ -365,6 +374,22 @@ def run_b200(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args, sample_length=args.cpu_sample_length, threads=os.cpu_count())
         cpu.pop("seconds", None)
+
+    # The other configurations, as blocks of the same line (the headline stays config 4).
+    blocks = {}
+    if not args.no_blocks:
+        del qs, ks, vs, dos, lses, out, grads
+        torch.cuda.empty_cache()
+        block_steps = max(5, min(args.steps, 20))
+        if world == 1:
+            blocks["cfg2"] = cfg2_block(device, block_steps, args.warmup, peak)
+            torch.cuda.empty_cache()
+        blocks["cfg3_batch_head"] = cfg3_block(device, world, rank, block_steps, args.warmup, peak, barrier,
+                                               max_over_ranks)
+        torch.cuda.empty_cache()
+        blocks["cfg5_seqshard"] = seqshard_block(device, world, rank, max(3, min(args.steps, 10)), args.warmup,
+                                                 peak)
+        torch.cuda.empty_cache()
 
     if rank == 0:
         line = {
@@ -386,6 +411,7 @@ def run_b200(args) -> None:
             "cpu_baseline": cpu,
             "gpu_launches": 2 * layers * args.steps,
         }
+        line.update(blocks)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -467,26 +493,127 @@ def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
                    "copies on two side streams overlapped with compute"}
 
 
-def run_seqshard(args) -> None:
-    """Config 5: one sequence of 4,194,304 positions x 22 layers in contiguous shards (strong scaling)."""
-    import datetime
+class L2Flush:
+    """Writes a 256 MiB buffer (more than the 126 MB L2) so the next step starts from DRAM."""
 
+    def __init__(self, device) -> None:
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        self.n = 0
+
+    def __call__(self) -> None:
+        self.n += 1
+        self.buf.fill_(self.n & 0xFF)
+
+
+def timed_steps(step, steps: int, warmup: int, flush: L2Flush | None) -> float:
+    """Mean CUDA-event time (ms) of ``step`` over ``steps`` runs after ``warmup`` untimed ones;
+    with ``flush``, L2 is flushed before every run, outside the event pair."""
+    for _ in range(max(3, warmup)):
+        step()
+    events = []
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        events.append((s, e))
+    torch.cuda.synchronize()
+    return statistics.mean(s.elapsed_time(e) for s, e in events)
+
+
+def _blhd(shape_blhd, device, gen, dtype=torch.bfloat16):
+    """q/k/v-like [B, H, L, D] view of a [B, L, H, D] tensor (the projections' layout)."""
+    return torch.randn(shape_blhd, device=device, dtype=dtype, generator=gen).permute(0, 2, 1, 3)
+
+
+def cfg2_block(device, steps: int, warmup: int, peak: float) -> dict:
+    """Config 2: one SBDA layer (l = 10: offsets 0, 1, 2, 512), B 4 x 8 heads x 64, L 32,768, bf16,
+    forward + backward; L2 flushed between steps (every tensor is ~134 MB, about the L2 size)."""
+    import sbda_b200
+    from sbda_b200 import ops
+
+    B, H, L, D = 4, 8, 32768, 64
+    offsets = sbda_b200.topology_offsets(10, topology="sbda")
+    gen = torch.Generator(device=device).manual_seed(10)
+    q, k, v, do = (_blhd((B, L, H, D), device, gen) for _ in range(4))
+    out, lse = torch.empty_like(q), torch.empty((B, H, L), device=device, dtype=torch.float32)
+    grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v))
+    flush = L2Flush(device)
+    fwd = lambda: ops.sbda_forward(q, k, v, offsets, out=out, lse=lse)  # noqa: E731
+    bwd = lambda: ops.sbda_backward(q, k, v, do, lse, offsets, grads=grads)  # noqa: E731
+    fwd_ms = timed_steps(fwd, steps, warmup, flush)
+    bwd_ms = timed_steps(bwd, steps, warmup, flush)
+    step_ms = timed_steps(lambda: (fwd(), bwd()), steps, warmup, flush)
+    rows = B * H * L
+    fb, bb = rows * (4 * D * 2 + 4), rows * (7 * D * 2 + 4)
+    return {
+        "workload": "cfg2: SBDA layer 10 (offsets 0,1,2,512), B 4 x 8 heads x 64, L 32768, bf16, fwd+bwd",
+        "value": B * L / (step_ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": step_ms,
+        "l2": "256 MiB buffer written before every timed step",
+        "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s",
+                     "fwd": {"ms": fwd_ms, "achieved": fb / (fwd_ms * 1e-3) / 1e9,
+                             "frac": fb / (fwd_ms * 1e-3) / 1e9 / peak, "algorithmic_bytes": fb},
+                     "bwd": {"ms": bwd_ms, "achieved": bb / (bwd_ms * 1e-3) / 1e9,
+                             "frac": bb / (bwd_ms * 1e-3) / 1e9 / peak, "algorithmic_bytes": bb},
+                     "step": {"achieved": (fb + bb) / (step_ms * 1e-3) / 1e9,
+                              "frac": (fb + bb) / (step_ms * 1e-3) / 1e9 / peak}},
+        "gpu_launches": 2 * steps,
+    }
+
+
+def cfg3_block(device, world: int, rank: int, steps: int, warmup: int, peak: float, barrier, max_over_ranks) -> dict:
+    """Config 3: the paper's training shape, B 8 x 8 heads x 64, L 32,768, 15 SBDA layers, bf16,
+    forward + backward of every attention layer, with the B x H (batch, head) sequences split into
+    contiguous ranges across the ranks (``sbda_b200.partition``; no data-path collective).  Total
+    work is fixed: strong scaling.  L2 flushed before every timed step."""
+    import sbda_b200
+    from sbda_b200.partition import partitioned_backward, partitioned_forward, unit_range
+
+    B, H, L, D, layers = 8, 8, 32768, 64, 15
+    offsets = [sbda_b200.topology_offsets(layer, topology="sbda", total_layers=layers)
+               for layer in range(1, layers + 1)]
+    gen = torch.Generator(device=device).manual_seed(300)
+    qs, ks, vs, dos = ([_blhd((B, L, H, D), device, gen) for _ in range(layers)] for _ in range(4))
+    lses = [torch.empty((B, H, L), device=device, dtype=torch.float32) for _ in range(layers)]
+    out = torch.empty_like(qs[0])
+    grads = (torch.empty_like(qs[0]), torch.empty_like(qs[0]), torch.empty_like(qs[0]))
+
+    def step():
+        for layer in range(layers):
+            partitioned_forward(qs[layer], ks[layer], vs[layer], offsets[layer], world, rank, out=out, lse=lses[layer])
+        for layer in reversed(range(layers)):
+            partitioned_backward(qs[layer], ks[layer], vs[layer], dos[layer], lses[layer], offsets[layer], world,
+                                 rank, grads=grads)
+
+    barrier()
+    ms = max_over_ranks(timed_steps(step, steps, warmup, L2Flush(device)))
+    lo, hi = unit_range(B, H, world, rank)
+    rank_bytes = (hi - lo) * L * layers * (11 * D * 2 + 8)
+    return {
+        "workload": (f"cfg3: 15 SBDA layers, B {B} x {H} heads x {D}, L {L}, bf16, fwd+bwd; (batch, head) "
+                     f"sequences split into {world} contiguous ranges"),
+        "value": B * L / (ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms, "scaling": "strong",
+        "units_per_rank": [unit_range(B, H, world, r)[1] - unit_range(B, H, world, r)[0] for r in range(world)],
+        "l2": "256 MiB buffer written before every timed step",
+        "roofline": {"bound": "hbm", "achieved_per_gpu": rank_bytes / (ms * 1e-3) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": rank_bytes / (ms * 1e-3) / 1e9 / peak},
+        "gpu_launches": 2 * layers * steps,
+    }
+
+
+def seqshard_block(device, world: int, rank: int, steps: int, warmup: int, peak: float, total: int = 1 << 22,
+                   heads: int = 4, head_dim: int = 64) -> dict:
+    """Config 5: one sequence of ``total`` positions x 22 SBDA layers in ``world`` contiguous shards
+    (strong scaling); the i - 2^(l-1) halos come from the owning GPU over NVLink inside the kernels.
+    One GPU runs the unsharded kernels on the whole sequence."""
     import torch.distributed as dist
 
     import sbda_b200
     from sbda_b200.sharded import ShardGroup, sharded_backward, sharded_forward
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    total, layers, H, D = 1 << 22, 22, args.heads, args.head_dim
-    if args.length != 1 << 20:
-        total = args.length
+    layers, H, D = 22, heads, head_dim
     shard = total // world
     shards = ShardGroup()
     offsets = sbda_b200.sbda_layer_offsets(layers)
@@ -506,49 +633,69 @@ def run_seqshard(args) -> None:
         for layer in reversed(range(layers)):
             sharded_backward(q, k, v, do, lses[layer], offsets[layer], shards)
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     end.record()
     torch.cuda.synchronize()
-    clocks = sampler.stop()
-    ms = start.elapsed_time(end) / args.steps
+    ms = start.elapsed_time(end) / steps
     if world > 1:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    peak, peak_kind = measured_peak_gbs()
+        shards.barrier()
+        torch.cuda.synchronize()
     step_bytes = total * H * layers * (11 * D * 2 + 8)
     link = shard_link_model(total, world, H, D, 2, offsets, peak)
     link["frac_of_target"] = link["target_ms"] / ms
-    if rank == 0:
-        print(json.dumps({
-            "metric": "SBDA attn fwd+bwd Mpositions/s, one 4M-position sequence x 22 layers in contiguous shards",
-            "value": total / (ms * 1e-3) / 1e6, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded, resident in HBM",
-            "config": {"workload": f"cfg5: {total} positions x {layers} layers, {H} heads x {D}, "
-                                   f"{world} contiguous shards of {shard}",
-                       "kernels": ("windowed (sbda_v2) kernels; 1 GPU: unsharded calls; N > 1: sharded calls "
-                                   "whose K/V tiles and halos past the shard are staged from the owning GPU over "
-                                   "NVLink with non-multicast TMA")},
-            "clocks": clocks,
-            "shard_link_model": link,
-            "step_roofline": {"achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": peak * world, "unit": "GB/s",
-                              "frac": step_bytes / (ms * 1e-3) / 1e9 / (peak * world), "peak_kind": peak_kind,
-                              "algorithmic_bytes_per_step": step_bytes},
-            "gpu_launches": 2 * layers * args.steps,
-        }), flush=True)
+    return {
+        "workload": f"cfg5: {total} positions x {layers} layers, {H} heads x {D}, {world} contiguous shards of {shard}",
+        "value": total / (ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms, "scaling": "strong",
+        "kernels": ("windowed (sbda_v2) kernels; 1 GPU: unsharded calls; N > 1: sharded calls whose K/V tiles and "
+                    "halos past the shard are staged from the owning GPU over NVLink with non-multicast TMA"),
+        "shard_link_model": link,
+        "step_roofline": {"achieved": step_bytes / (ms * 1e-3) / 1e9, "peak": peak * world, "unit": "GB/s",
+                          "frac": step_bytes / (ms * 1e-3) / 1e9 / (peak * world),
+                          "algorithmic_bytes_per_step": step_bytes},
+        "gpu_launches": 2 * layers * steps,
+    }
+
+
+def run_seqshard(args) -> None:
+    """``--workload cfg5``: the config-5 line on its own (strong scaling over the torchrun ranks)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
     if world > 1:
-        shards.barrier()
-        torch.cuda.synchronize()
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    peak, peak_kind = measured_peak_gbs()
+    total = 1 << 22 if args.length == 1 << 20 else args.length
+    sampler = ClockSampler(local)
+    block = seqshard_block(device, world, rank, args.steps, args.warmup, peak, total=total, heads=args.heads,
+                           head_dim=args.head_dim)
+    clocks = sampler.stop()
+    if rank == 0:
+        line = {"metric": "SBDA attn fwd+bwd Mpositions/s, one 4M-position sequence x 22 layers in contiguous shards",
+                "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "higher_is_better": True,
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded, resident in HBM",
+                "clocks": clocks, "peak_kind": peak_kind}
+        line.update(block)
+        line["config"] = {"workload": line.pop("workload"), "kernels": line.pop("kernels")}
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
 
 
