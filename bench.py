@@ -96,11 +96,11 @@ def measured_peak_gbs() -> tuple[float, str]:
 
 # DRAM bytes per (batch, head, position) row of one windowed backward launch (dram__bytes_read.sum
 # + dram__bytes_write.sum), measured by ncu on a small case of the same kernel: 262,144 positions
-# x 4 heads x 64, bf16, layers 4, 10 and 19 (local, chain and long-chain walks), averaged over the
-# three launches.  Traffic grows in proportion to the rows, so a full launch's traffic is this
-# figure times its rows.  The capture command and its figures are in
-# profiles/sbda_bwd_kernel_small_case.md.  None until measured.
-BWD_DRAM_BYTES_PER_ROW: float | None = None
+# x 4 heads x 64, bf16, layers 4, 10 and 17 (local and chain walks), averaged over the three
+# launches.  Traffic grows in proportion to the rows, so a full launch's traffic is this figure
+# times its rows.  The capture command and the per-launch figures are in
+# profiles/sbda_bwd_kernel_small_case.md.
+BWD_DRAM_BYTES_PER_ROW: float | None = 884.2
 
 
 def backward_traffic(rows: int) -> float | None:

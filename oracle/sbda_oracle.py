@@ -396,6 +396,79 @@ def module_forward(x: Tensor, params: dict[str, Tensor], *, heads: int, layer: i
 
 
 # ---------------------------------------------------------------------------
+# Whole LM as dense causal attention (an independent evaluation of BiAttn/model.py:248-502)
+# ---------------------------------------------------------------------------
+
+
+def dense_source_mask(length: int, offsets: Sequence[int], device=None) -> Tensor:
+    """Boolean ``[L, L]`` attention mask of a layer: query ``i`` may attend key ``j`` iff
+    ``i - j`` is one of the layer's offsets (so ``j <= i``: a causal mask thinned to the sources)."""
+    pos = torch.arange(length, device=device)
+    delta = pos[:, None] - pos[None, :]
+    allowed = torch.zeros(length, length, dtype=torch.bool, device=device)
+    for o in offsets:
+        allowed |= delta == int(o)
+    return allowed
+
+
+def lm_forward_dense(ids: Tensor, params: dict[str, Tensor], config: dict,
+                     valid_mask: Tensor | None = None) -> Tensor:
+    """``BiAttnLM.forward_hidden`` (MHA, dense SwiGLU, untied or tied head) followed by the
+    vocabulary head, with every attention layer evaluated as dense scaled-dot-product attention
+    over the whole causal square, masked to the layer's sources.
+
+    Same function as the reference's gather path (``left_v2.py:335-405``: softmax over the
+    sources, ``D**-0.5`` scale), computed by a different algorithm -- the dense causal
+    cross-check of config 1.  ``params`` holds the reference's state-dict keys; ``valid_mask``
+    must be a prefix mask (``model.py:323-335`` multiplies the attention and feed-forward
+    outputs by it).  Returns logits ``[B, L, vocab]``.
+    """
+    import torch.nn.functional as F
+
+    dim, heads, layers = config["dim"], config["heads"], config["layers"]
+    theta = float(config.get("rope_theta", 1_000_000.0))
+    topology = "sbda" if config.get("attention_backend") == "sbda" else config.get("path_topology", "binary")
+    batch, length = ids.shape
+    head_dim = dim // heads
+    mask = None if valid_mask is None or bool(valid_mask.all()) else valid_mask[:, :, None]
+    x = F.embedding(ids, params["embedding.weight"])
+    for i in range(layers):
+        pre = f"layers.{i}."
+        a = pre + "attn."
+        n1 = F.rms_norm(x, (dim,), params[pre + "norm1.weight"], 1e-6)
+        q = F.linear(n1, params[a + "q.weight"]).view(batch, length, heads, head_dim)
+        k = F.linear(n1, params[a + "k.weight"]).view(batch, length, heads, head_dim)
+        v = F.linear(n1, params[a + "v.weight"]).view(batch, length, heads, head_dim)
+        q = head_rms_norm(q, params[a + "q_norm.weight"])
+        k = head_rms_norm(k, params[a + "k_norm.weight"])
+        if head_dim % 2 == 0:
+            pos = torch.arange(length, device=ids.device)
+            inv = theta ** (-torch.arange(0, head_dim, 2, device=ids.device, dtype=torch.float32) / head_dim)
+            ang = torch.outer(pos.to(torch.float32), inv)
+            cos = torch.cat((ang.cos(), ang.cos()), -1)[None, :, None, :].to(q.dtype)
+            sin = torch.cat((ang.sin(), ang.sin()), -1)[None, :, None, :].to(q.dtype)
+            q, k = q * cos + rotate_half(q) * sin, k * cos + rotate_half(k) * sin
+        offsets = schedule_offsets(i + 1, topology, layers)
+        attn_mask = dense_source_mask(length, offsets, ids.device)
+        att = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                             attn_mask=attn_mask)
+        out = F.linear(att.transpose(1, 2).reshape(batch, length, dim), params[a + "out.weight"])
+        if mask is not None:
+            out = out * mask.to(out.dtype)
+        x = x + out
+        n2 = F.rms_norm(x, (dim,), params[pre + "norm2.weight"], 1e-6)
+        f = pre + "ff."
+        hidden = F.silu(F.linear(n2, params[f + "gate.weight"], params.get(f + "gate.bias"))) * \
+            F.linear(n2, params[f + "up.weight"], params.get(f + "up.bias"))
+        ff = F.linear(hidden, params[f + "down.weight"], params.get(f + "down.bias"))
+        if mask is not None:
+            ff = ff * mask.to(ff.dtype)
+        x = x + ff
+    h = F.rms_norm(x, (dim,), params["norm.weight"], 1e-6)
+    return F.linear(h, params["lm_head.weight"])
+
+
+# ---------------------------------------------------------------------------
 # Byte model used by the roofline (not a reference quantity)
 # ---------------------------------------------------------------------------
 
@@ -414,6 +487,6 @@ __all__ = [
     "ORACLE_TOPOLOGIES", "unique_offsets", "schedule_offsets", "sbda_stage", "path_tensors",
     "exact_attention", "exact_lse", "exact_attention_grads", "query_rows", "key_rows", "head_rms_norm",
     "rope_inverse_frequencies", "rope_cos_sin", "rotate_half", "apply_rope", "apply_rope_table", "norm_rope",
-    "module_forward", "algorithmic_bytes",
+    "module_forward", "dense_source_mask", "lm_forward_dense", "algorithmic_bytes",
 ]
 

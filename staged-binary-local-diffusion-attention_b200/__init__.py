@@ -23,7 +23,7 @@ from .norm_rope import norm_rope, rope_table
 from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_offsets
 
 __all__ = [
-    "BiAttnBlock", "BinaryPathAttention", "PATH_TOPOLOGIES", "RMSNorm", "SBDAttention", "SwiGLU",
+    "BiAttnBlock", "BiAttnConfig", "BiAttnLM", "BinaryPathAttention", "PATH_TOPOLOGIES", "RMSNorm", "SBDAttention", "SwiGLU",
     "add_rms_norm", "rms_norm", "silu_mul", "SBDAAttention", "current_family", "device_status", "kernel_family", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
     "fused_sbda_key_backward", "host_offsets", "norm_rope", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
@@ -36,6 +36,10 @@ def __getattr__(name: str):
         from . import attention
 
         return getattr(attention, name)
+    if name in ("BiAttnConfig", "BiAttnLM", "FactorizedTokenIO"):
+        from . import model
+
+        return getattr(model, name)
     if name in ("BiAttnBlock", "RMSNorm", "SwiGLU", "add_rms_norm", "rms_norm", "silu_mul"):
         from . import block
 

@@ -56,6 +56,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return g_encode;
 }
 
+// The tensor-map encoder is a driver call and needs a current context on the
+// calling thread.  A thread that has only run cached runtime calls (autograd's
+// worker thread on its first backward, for instance) may have none yet: bind
+// the current device's primary context, so the caller can retry the encode.
+bool bind_current_context() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess;
+}
+
 int elem_size(int dtype) { return dtype == SBDA_DTYPE_F32 ? 4 : 2; }
 
 CUtensorMapDataType map_dtype(int dtype) {
@@ -133,9 +142,13 @@ bool encode_map(CUtensorMap* map, unsigned* slots, const sbda_tensor& t, int dty
     }
   }
   *slots = s;
-  const CUresult r = enc(map, map_dtype(dtype), 4, const_cast<void*>(t.data), gdim, gstride, box, estride,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto encode = [&] {
+    return enc(map, map_dtype(dtype), 4, const_cast<void*>(t.data), gdim, gstride, box, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r != CUDA_SUCCESS && bind_current_context()) r = encode();
   return r == CUDA_SUCCESS;
 }
 
@@ -148,9 +161,14 @@ bool encode_lse_map(CUtensorMap* map, const float* lse, int64_t rows, int64_t L,
   cuuint64_t gstride[1] = {(cuuint64_t)(L * 4)};
   cuuint32_t boxd[2] = {(cuuint32_t)box, 1};
   cuuint32_t estride[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(lse), gdim, gstride, boxd, estride,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  auto encode = [&] {
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(lse), gdim, gstride, boxd, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r != CUDA_SUCCESS && bind_current_context()) r = encode();
+  return r == CUDA_SUCCESS;
 }
 
 // Splits offsets into the near window and at most one far offset for a tile

@@ -22,6 +22,7 @@ def pytest_configure(config):
 
 PATH_GOLDEN = os.path.join(ROOT, "tests", "golden", "path_golden.npz")
 BLOCK_GOLDEN = os.path.join(ROOT, "tests", "golden", "block_golden.npz")
+LM_GOLDEN = os.path.join(ROOT, "tests", "golden", "lm_golden.npz")
 
 
 class Golden:
@@ -53,3 +54,8 @@ def path_golden() -> Golden:
 @pytest.fixture(scope="session")
 def block_golden() -> Golden:
     return Golden(BLOCK_GOLDEN)
+
+
+@pytest.fixture(scope="session")
+def lm_golden() -> Golden:
+    return Golden(LM_GOLDEN)
