@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("cfg4", "cfg5", "block"), default="cfg4",
+    p.add_argument("--workload", choices=("cfg4", "cfg5", "block", "normed"), default="cfg4",
                    help="cfg4 (default, the metric): one 1M-position sequence per GPU; cfg5: one "
                         "4M-position, 22-layer sequence split into contiguous shards across the GPUs")
     p.add_argument("--length", type=int, default=1 << 20)
@@ -384,6 +384,9 @@ def run_b200(args) -> None:
         if world == 1:
             blocks["cfg2"] = cfg2_block(device, block_steps, args.warmup, peak)
             torch.cuda.empty_cache()
+            blocks["cfg4_norm_rope_attention"] = norm_rope_attention_block(device, max(3, min(args.steps, 10)),
+                                                                           args.warmup, peak)
+            torch.cuda.empty_cache()
         blocks["cfg3_batch_head"] = cfg3_block(device, world, rank, block_steps, args.warmup, peak, barrier,
                                                max_over_ranks)
         torch.cuda.empty_cache()
@@ -560,6 +563,68 @@ def cfg2_block(device, steps: int, warmup: int, peak: float) -> dict:
                      "step": {"achieved": (fb + bb) / (step_ms * 1e-3) / 1e9,
                               "frac": (fb + bb) / (step_ms * 1e-3) / 1e9 / peak}},
         "gpu_launches": 2 * steps,
+    }
+
+
+def norm_rope_attention_block(device, steps: int, warmup: int, peak: float, length: int = 1 << 20, heads: int = 4,
+                              layers: int = 20) -> dict:
+    """Config 4 with the q/k per-head RMSNorm + RoPE in the step (what ``SBDAttention`` runs
+    between its projections and its output projection), forward + backward of all 20 layers, two
+    routes on the same seeded inputs through the public API:
+
+    * fused: ``normed_attention`` -- one kernel each way, norm + RoPE inside the attention kernels;
+    * separate: ``norm_rope`` on q and on k, then ``fused_sbda_key_backward`` -- five kernels each
+      way, the normalised q / k written to and read back from HBM.
+
+    Algorithmic bytes per (position, head) row: fused 1,416 (the attention's; q/k arrive raw and
+    dq/dk leave raw); separate adds norm + RoPE forward (read and write q and k: 4 x 128 B) and
+    backward (read x and dy, write dx for q and k: 6 x 128 B) for 2,696."""
+    import sbda_b200
+
+    D = 64
+    offsets = sbda_b200.sbda_layer_offsets(layers)
+    gen = torch.Generator(device=device).manual_seed(400)
+    qs, ks, vs, dos = ([_blhd((1, length, heads, D), device, gen) for _ in range(layers)] for _ in range(4))
+    wq = torch.rand(D, device=device, generator=gen) + 0.5
+    wk = torch.rand(D, device=device, generator=gen) + 0.5
+    for layer in range(layers):
+        if not sbda_b200.normed_supported(qs[layer], ks[layer], vs[layer], offsets[layer]):
+            raise RuntimeError(f"layer {layer + 1} is not served by the fused kernels")
+
+    def fused():
+        for layer in range(layers):
+            q, k, v = (t.detach().requires_grad_() for t in (qs[layer], ks[layer], vs[layer]))
+            w1, w2 = wq.detach().requires_grad_(), wk.detach().requires_grad_()
+            sbda_b200.normed_attention(q, k, v, w1, w2, offsets[layer]).backward(dos[layer])
+
+    def separate():
+        for layer in range(layers):
+            q, k, v = (t.detach().requires_grad_() for t in (qs[layer], ks[layer], vs[layer]))
+            w1, w2 = wq.detach().requires_grad_(), wk.detach().requires_grad_()
+            qn = sbda_b200.norm_rope(q.permute(0, 2, 1, 3), w1).permute(0, 2, 1, 3)
+            kn = sbda_b200.norm_rope(k.permute(0, 2, 1, 3), w2).permute(0, 2, 1, 3)
+            sbda_b200.fused_sbda_key_backward(qn, kn, v, offsets[layer]).backward(dos[layer])
+
+    fused_ms = timed_steps(fused, steps, warmup, None)
+    separate_ms = timed_steps(separate, steps, warmup, None)
+    rows = length * heads * layers
+    fused_bytes, separate_bytes = rows * (11 * D * 2 + 8), rows * (21 * D * 2 + 8)
+    return {
+        "workload": (f"cfg4 + per-head RMSNorm + RoPE of q and k: {length} positions x {layers} layers, {heads} "
+                     f"heads x {D}, bf16, fwd+bwd through the public API"),
+        "value": length / (fused_ms * 1e-3) / 1e6, "unit": UNIT,
+        "fused_ms_per_step": fused_ms, "separate_ms_per_step": separate_ms,
+        "speedup_fused_vs_separate": separate_ms / fused_ms,
+        "separate_Mpositions_s": length / (separate_ms * 1e-3) / 1e6,
+        "l2": "every tensor 512 MiB > 126 MB L2",
+        "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s",
+                     "fused": {"algorithmic_bytes_per_step": fused_bytes,
+                               "achieved": fused_bytes / (fused_ms * 1e-3) / 1e9,
+                               "frac": fused_bytes / (fused_ms * 1e-3) / 1e9 / peak},
+                     "separate": {"algorithmic_bytes_per_step": separate_bytes,
+                                  "achieved": separate_bytes / (separate_ms * 1e-3) / 1e9,
+                                  "frac": separate_bytes / (separate_ms * 1e-3) / 1e9 / peak}},
+        "gpu_launches": {"fused": (2 + 2) * layers * steps, "separate": (2 + 2 + 2 + 2 * 2) * layers * steps},
     }
 
 
@@ -781,6 +846,12 @@ def main() -> None:
         run_seqshard(args)
     elif args.workload == "block":
         run_block(args)
+    elif args.workload == "normed":
+        torch.cuda.set_device(0)
+        peak, _ = measured_peak_gbs()
+        block = norm_rope_attention_block(torch.device("cuda", 0), args.steps, args.warmup, peak, length=args.length,
+                                          heads=args.heads, layers=args.layers)
+        print(json.dumps(block), flush=True)
     else:
         run_b200(args)
 

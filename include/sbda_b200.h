@@ -186,6 +186,52 @@ int sbda_b200_norm_rope_backward_noalloc(int dtype, sbda_shape shape, sbda_tenso
                                          sbda_tensor grad_x, float* grad_weight, void* stream);
 
 /*
+ * Attention with the per-head RMSNorm + RoPE of q and k inside the kernels.
+ * Replaces, on the reference's fused route, _HeadRMSNorm and _apply_rope
+ * (BiAttn/attention_common.py:13-76, applied at BiAttn/left_v2.py:237-239)
+ * followed by fused_sbda_key_backward (sbda_triton.py:1467-1474): one kernel
+ * each way instead of five.  q_raw / k_raw are the projections before the
+ * norm ([B, H, L, D] views, like q / k above).  Each row is normalised in
+ * fp32 (r = rsqrt(mean(x^2) + eps), y = cast(x * r * w)) and rotated in the
+ * element type (z = cast(cast(y * cos) + cast(rotate_half(y) * sin))), with
+ * cos_table / sin_table the [rows, D / 2] tables of the element type and row
+ * table_offset + l serving position l.  Weights are fp32 [D], 16-byte aligned.
+ *
+ * Served (sbda_b200_normed_supported() == 1): head_dim 64, heads == kv_heads,
+ * fp32 / fp16 / bf16, near offsets within {0, 1, 2} with at most one far
+ * offset in the SBDA family's sets {0,1}, {0,2}, {0,1,2,d}, and views the copy
+ * engine can stage (16-byte aligned rows and strides); other calls return
+ * SBDA_ERR_UNSUPPORTED and the caller runs norm_rope + attention separately.
+ */
+int sbda_b200_normed_supported(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets);
+
+int sbda_b200_forward_normed(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                             float scale, sbda_tensor q_raw, sbda_tensor k_raw, sbda_tensor v,
+                             const float* q_weight, float q_eps, const float* k_weight, float k_eps,
+                             const void* cos_table, const void* sin_table, int64_t table_offset,
+                             sbda_tensor out, float* lse, void* stream);
+
+/* fp32 workspace floats of sbda_b200_backward_normed (per-CTA weight-gradient
+ * partials and their first reduction level); -1 if the call is not served. */
+int64_t sbda_b200_backward_normed_workspace_floats(int dtype, sbda_shape shape, const int32_t* offsets,
+                                                   int32_t n_offsets);
+
+/*
+ * Backward of sbda_b200_forward_normed: writes grad_q / grad_k with respect to
+ * q_raw / k_raw (the RoPE transpose and the RMSNorm Jacobian applied in the
+ * kernel), grad_v, and the fp32 [D] norm-weight gradients grad_q_weight /
+ * grad_k_weight (summed over every row in a fixed order: deterministic).
+ */
+int sbda_b200_backward_normed(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                              float scale, sbda_tensor q_raw, sbda_tensor k_raw, sbda_tensor v,
+                              sbda_tensor grad_out, const float* lse, const float* q_weight, float q_eps,
+                              const float* k_weight, float k_eps, const void* cos_table,
+                              const void* sin_table, int64_t table_offset, sbda_tensor grad_q,
+                              sbda_tensor grad_k, sbda_tensor grad_v, float* grad_q_weight,
+                              float* grad_k_weight, float* workspace, int64_t workspace_floats,
+                              void* stream);
+
+/*
  * Forward / backward with a per-row source mask, for rows whose usable sources
  * depend on the data: padding holes and segment (seam) resets.
  * source_mask[b * length + i], bit s set: source s of row i may be used (on

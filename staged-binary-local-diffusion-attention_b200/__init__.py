@@ -19,14 +19,14 @@ from .ops import (
     sbda_backward,
     sbda_forward,
 )
-from .norm_rope import norm_rope, rope_table
+from .norm_rope import norm_rope, normed_attention, normed_supported, rope_table
 from .topology import PATH_TOPOLOGIES, sbda_layer_offsets, sbda_stage, topology_offsets
 
 __all__ = [
     "BiAttnBlock", "BiAttnConfig", "BiAttnLM", "BinaryPathAttention", "PATH_TOPOLOGIES", "RMSNorm", "SBDAttention", "SwiGLU",
     "add_rms_norm", "rms_norm", "silu_mul", "SBDAAttention", "current_family", "device_status", "kernel_family", "fused_sbda",
     "fused_sbda_block", "fused_sbda_block_full", "fused_sbda_gqa_key_backward",
-    "fused_sbda_key_backward", "host_offsets", "norm_rope", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
+    "fused_sbda_key_backward", "host_offsets", "norm_rope", "normed_attention", "normed_supported", "rope_table", "sbda_attention", "sbda_backward", "sbda_forward",
     "sbda_layer_offsets", "sbda_stage", "topology_offsets",
 ]
 

@@ -159,6 +159,22 @@ def load() -> ctypes.CDLL:
             tarr, tarr, tarr, tarr, ctypes.POINTER(c_void_p),
             SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
         ]
+        lib.sbda_b200_normed_supported.restype = c_int
+        lib.sbda_b200_normed_supported.argtypes = [c_int, SbdaShape, i32p, c_int32]
+        lib.sbda_b200_forward_normed.restype = c_int
+        lib.sbda_b200_forward_normed.argtypes = [
+            c_int, SbdaShape, i32p, c_int32, c_float, SbdaTensor, SbdaTensor, SbdaTensor,
+            c_void_p, c_float, c_void_p, c_float, c_void_p, c_void_p, ctypes.c_int64, SbdaTensor, c_void_p,
+            c_void_p,
+        ]
+        lib.sbda_b200_backward_normed_workspace_floats.restype = ctypes.c_int64
+        lib.sbda_b200_backward_normed_workspace_floats.argtypes = [c_int, SbdaShape, i32p, c_int32]
+        lib.sbda_b200_backward_normed.restype = c_int
+        lib.sbda_b200_backward_normed.argtypes = [
+            c_int, SbdaShape, i32p, c_int32, c_float, SbdaTensor, SbdaTensor, SbdaTensor, SbdaTensor, c_void_p,
+            c_void_p, c_float, c_void_p, c_float, c_void_p, c_void_p, ctypes.c_int64, SbdaTensor, SbdaTensor,
+            SbdaTensor, c_void_p, c_void_p, c_void_p, ctypes.c_int64, c_void_p,
+        ]
         fwd_args = lib.sbda_b200_forward.argtypes
         bwd_args = lib.sbda_b200_backward.argtypes
         lib.sbda_b200_forward_ex.restype = c_int

@@ -1027,3 +1027,164 @@ extern "C" int sbda_b200_backward_sharded(int dtype, sbda_shape shape, const int
   return sbda_b200_backward_sharded_ex(kFamilyAuto, dtype, shape, offsets, n_offsets, scale, rank, world, q_ranks,
                                        k_ranks, v_ranks, grad_out_ranks, lse_ranks, grad_q, grad_k, grad_v, stream);
 }
+
+// --------------------------------------------------------------------------
+// Attention with the per-head RMSNorm + RoPE of q and k fused in
+// --------------------------------------------------------------------------
+
+namespace sbda {
+
+// Shape-level eligibility of the fused entry points; fills the plan.
+int normed_plan(int dtype, const sbda_shape& shape, const int32_t* offsets, int n, V2Plan* p2) {
+  const int st = validate(dtype, shape, offsets, n);
+  if (st != SBDA_OK) return st;
+  if (shape.head_dim != 64 || shape.heads != shape.kv_heads) return SBDA_ERR_UNSUPPORTED;
+  if (shape.batch == 0 || shape.heads == 0 || shape.length == 0) return SBDA_OK;
+  if (!plan_v2(offsets, n, shape.length, shape.head_dim, elem_size(dtype), 1, shape.batch, shape.heads, p2))
+    return SBDA_ERR_UNSUPPORTED;
+  return v2_normed_plan_ok(*p2) ? SBDA_OK : SBDA_ERR_UNSUPPORTED;
+}
+
+// Norm weights (fp32 [64], 16-byte aligned) and tables ([rows, 32] in the
+// element type, 16-byte aligned) of one tensor.
+int normed_args(NormRopeArgs* a, const float* w, float eps, const void* cos_t, const void* sin_t,
+                int64_t table_offset) {
+  if (!w || !cos_t || !sin_t || table_offset < 0) return SBDA_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(cos_t) % 16 ||
+      reinterpret_cast<uintptr_t>(sin_t) % 16)
+    return SBDA_ERR_UNSUPPORTED;
+  if (!(eps >= 0.f)) return SBDA_ERR_INVALID;
+  a->w = w;
+  a->cos_t = cos_t;
+  a->sin_t = sin_t;
+  a->table_offset = table_offset;
+  a->eps = eps;
+  return SBDA_OK;
+}
+
+}  // namespace sbda
+
+extern "C" int sbda_b200_normed_supported(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets) {
+  V2Plan p2;
+  return normed_plan(dtype, shape, offsets, n_offsets, &p2) == SBDA_OK ? 1 : 0;
+}
+
+extern "C" int sbda_b200_forward_normed(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                        float scale, sbda_tensor q_raw, sbda_tensor k_raw, sbda_tensor v,
+                                        const float* q_weight, float q_eps, const float* k_weight, float k_eps,
+                                        const void* cos_table, const void* sin_table, int64_t table_offset,
+                                        sbda_tensor out, float* lse, void* stream) {
+  V2Plan p2;
+  int st = normed_plan(dtype, shape, offsets, n_offsets, &p2);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, L = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || L == 0) return SBDA_OK;
+  if (!q_raw.data || !k_raw.data || !v.data || !out.data || !lse) return SBDA_ERR_INVALID;
+  FwdV2Params p;
+  memset(&p, 0, sizeof(p));
+  if ((st = normed_args(&p.nq, q_weight, q_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
+  if ((st = normed_args(&p.nk, k_weight, k_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
+  const int e = elem_size(dtype);
+  if (!tensors_vector_ok({&q_raw, &k_raw, &v, &out}, B, L, D, e, {H, H, H, H})) return SBDA_ERR_UNSUPPORTED;
+  p.B = (int)B;
+  p.H = (int)H;
+  p.L = (int)L;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = p2.g;
+  p.q = arg_of(q_raw);
+  p.k = arg_of(k_raw);
+  p.v = arg_of(v);
+  p.out = arg_of(out);
+  p.lse = lse;
+  p.status = status_ptr();
+  p.sh = single_shard(L, lse);
+  FwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  unsigned dummy;
+  const int lead = fwd_window_lead(p2.g, p2.tile);
+  if (!(encode_map(&maps.qT, &p.slots_q, q_raw, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.kT, &p.slots_k, k_raw, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.kH, &dummy, k_raw, dtype, B, H, L, D, p2.pitch, lead) &&
+        encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, lead)))
+    return SBDA_ERR_UNSUPPORTED;
+  return v2_forward_normed(dtype, maps, p, p2, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t sbda_b200_backward_normed_workspace_floats(int dtype, sbda_shape shape, const int32_t* offsets,
+                                                              int32_t n_offsets) {
+  V2Plan p2;
+  if (normed_plan(dtype, shape, offsets, n_offsets, &p2) != SBDA_OK) return -1;
+  if (shape.batch == 0 || shape.heads == 0 || shape.length == 0) return 0;
+  return v2_normed_workspace_floats(p2.blocks_bwd);
+}
+
+extern "C" int sbda_b200_backward_normed(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                         float scale, sbda_tensor q_raw, sbda_tensor k_raw, sbda_tensor v,
+                                         sbda_tensor grad_out, const float* lse, const float* q_weight, float q_eps,
+                                         const float* k_weight, float k_eps, const void* cos_table,
+                                         const void* sin_table, int64_t table_offset, sbda_tensor grad_q,
+                                         sbda_tensor grad_k, sbda_tensor grad_v, float* grad_q_weight,
+                                         float* grad_k_weight, float* workspace, int64_t workspace_floats,
+                                         void* stream) {
+  V2Plan p2;
+  int st = normed_plan(dtype, shape, offsets, n_offsets, &p2);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, L = shape.length, D = shape.head_dim;
+  if (!grad_q_weight || !grad_k_weight) return SBDA_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (B == 0 || H == 0 || L == 0) {  // empty: the weight gradients are zero
+    if (cudaMemsetAsync(grad_q_weight, 0, 64 * sizeof(float), s) != cudaSuccess ||
+        cudaMemsetAsync(grad_k_weight, 0, 64 * sizeof(float), s) != cudaSuccess)
+      return SBDA_ERR_CUDA;
+    return SBDA_OK;
+  }
+  if (!q_raw.data || !k_raw.data || !v.data || !grad_out.data || !lse || !grad_q.data || !grad_k.data ||
+      !grad_v.data || !workspace)
+    return SBDA_ERR_INVALID;
+  if (workspace_floats < v2_normed_workspace_floats(p2.blocks_bwd)) return SBDA_ERR_INVALID;
+  BwdV2Params p;
+  memset(&p, 0, sizeof(p));
+  if ((st = normed_args(&p.nq, q_weight, q_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
+  if ((st = normed_args(&p.nk, k_weight, k_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
+  const int e = elem_size(dtype);
+  if (!tensors_vector_ok({&q_raw, &k_raw, &v, &grad_out, &grad_q, &grad_k, &grad_v}, B, L, D, e,
+                         {H, H, H, H, H, H, H}))
+    return SBDA_ERR_UNSUPPORTED;
+  p.B = (int)B;
+  p.H = (int)H;
+  p.L = (int)L;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = p2.g;
+  p.q = arg_of(q_raw);
+  p.k = arg_of(k_raw);
+  p.v = arg_of(v);
+  p.dout = arg_of(grad_out);
+  p.dq = arg_of(grad_q);
+  p.dk = arg_of(grad_k);
+  p.dv = arg_of(grad_v);
+  p.lse = lse;
+  p.status = status_ptr();
+  p.sh = single_shard(L, lse);
+  p.lse_box = p2.lse_box;
+  p.lse_tx = p2.lse_box * 4;
+  p.dw_partial = workspace;
+  BwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  unsigned dummy;
+  const int hz = p2.g.halo;
+  const int lead = p2.g.mode == 2 ? p2.g.d : hz;
+  if (!(encode_map(&maps.qT, &p.slots_q, q_raw, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.kT, &p.slots_k, k_raw, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.qH, &dummy, q_raw, dtype, B, H, L, D, p2.pitch, hz) &&
+        encode_map(&maps.dH, &dummy, grad_out, dtype, B, H, L, D, p2.pitch, hz) &&
+        encode_map(&maps.kH, &dummy, k_raw, dtype, B, H, L, D, p2.pitch, lead) &&
+        encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, lead)))
+    return SBDA_ERR_UNSUPPORTED;
+  p.lse_tma = encode_lse_map(&maps.lseT, lse, B * H, L, p2.lse_box);
+  return v2_backward_normed(dtype, maps, p, p2, grad_q_weight, grad_k_weight, workspace, s);
+}

@@ -590,6 +590,17 @@ struct V2Geometry {
   int chains;            // backward chain walks per (b, h): min(R, nT)
 };
 
+// Per-head RMSNorm + RoPE of q or k applied inside the windowed kernels (the
+// *_normed entry points): fp32 weight [D], the cos/sin table [rows, D / 2] in
+// the element type, and the table row of local position 0.
+struct NormRopeArgs {
+  const float* w;
+  const void* cos_t;
+  const void* sin_t;
+  long long table_offset;
+  float eps;
+};
+
 struct FwdV2Params {
   int B, H, L, D;        // L: positions of this call's rows (the shard when sharded)
   float scale;
@@ -599,6 +610,7 @@ struct FwdV2Params {
   unsigned slots_q, slots_k, slots_v;
   unsigned* status;
   ShardInfo sh;          // one shard (pos0 = 0, total_len = L) unless sequence-sharded
+  NormRopeArgs nq, nk;   // normed kernels only: q and k arrive raw
 };
 
 struct BwdV2Params {
@@ -613,6 +625,8 @@ struct BwdV2Params {
   int lse_box;   // rows of an LSE slot in shared memory (Q/dO slot height rounded up to 32)
   int lse_tx;    // bytes the LSE copies of one step deliver
   ShardInfo sh;  // one shard (pos0 = 0, total_len = L) unless sequence-sharded
+  NormRopeArgs nq, nk;  // normed kernels only: q and k arrive raw, dq and dk leave raw
+  float* dw_partial;    // normed kernels only: [gridDim.x, 2, 64] per-CTA norm-weight gradients (q, k)
 };
 
 // Uniform kernels (sbda_v3.cu): every source a shifted tile.
@@ -676,5 +690,12 @@ int v3_forward(int dtype, bool tma, const FwdMaps& maps, const V3Params& p, cons
 int v3_backward(int dtype, bool tma, const BwdMaps& maps, const V3Params& p, const V3Plan& pl, cudaStream_t st);
 int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl,
                 cudaStream_t st);
+
+// Windowed kernels with the per-head RMSNorm + RoPE fused in (sbda_v2_normed.cu).
+bool v2_normed_plan_ok(const V2Plan& pl);
+int v2_forward_normed(int dtype, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st);
+int64_t v2_normed_workspace_floats(unsigned blocks);
+int v2_backward_normed(int dtype, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, float* grad_q_w,
+                       float* grad_k_w, float* workspace, cudaStream_t st);
 
 }  // namespace sbda

@@ -23,7 +23,7 @@
 // column sums and writes them once, so the final reduction is short and
 // its order is fixed.
 
-#include "sbda_common.cuh"
+#include "sbda_v2_kernels.cuh"  // norm_rope_frag / norm_rope_grad (head_dim 64, 8 lanes per row)
 
 #include <atomic>
 
@@ -226,8 +226,157 @@ __global__ void sbda_norm_weight_reduce_kernel(const float* __restrict__ partial
   dw[j] = acc;
 }
 
+// --------------------------------------------------------------------------
+// head_dim 64 with layouts the vector path takes (16-byte aligned rows and
+// strides, unit channel stride, 16-byte aligned tables and weight): 8 lanes
+// per row, each lane holding 8 channels in registers, the rotation partner
+// one shuffle away (lane ^ 4).  A CTA iteration covers 64 rows: row group g
+// takes rows base + 16 i + g (i = 0..3), so each warp reads 4 consecutive
+// rows (512 contiguous bytes in the [B, L, H, D] layout) per load, and a lane
+// has 4 loads in flight before it computes.
+// --------------------------------------------------------------------------
+
+constexpr int kNR64Rows = 64;  // rows per CTA iteration
+
+// n / d for 0 <= n < 2^31 by a multiply and a shift: division by an invariant
+// integer with a rounded-up multiplier (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994, theorem 4.2): with
+// l = ceil(log2 d) and m = ceil(2^(31 + l) / d) < 2^32, n / d = (n * m) >> (31 + l).
+struct FastDiv {
+  unsigned d, m, shift;
+};
+
+FastDiv make_fastdiv(unsigned d) {
+  unsigned l = 0;
+  while ((1ull << l) < d) ++l;
+  const unsigned long long num = 1ull << (31 + l);
+  return FastDiv{d, (unsigned)((num + d - 1) / d), 31 + l};
+}
+
+__device__ __forceinline__ unsigned fdiv(unsigned n, const FastDiv& f) {
+  return (unsigned)(((unsigned long long)n * f.m) >> f.shift);
+}
+
+// Row r of the (batch, position, head) order -> element offset in t and position.
+__device__ __forceinline__ void nr_coords(unsigned row, const FastDiv& fh, const FastDiv& fl, int* b, int* pos,
+                                          int* h) {
+  const unsigned bl = fdiv(row, fh);
+  *h = (int)(row - bl * fh.d);
+  const unsigned bb = fdiv(bl, fl);
+  *pos = (int)(bl - bb * fl.d);
+  *b = (int)bb;
+}
+
+__device__ __forceinline__ long long nr_offset(const TensorArg& t, int b, int pos, int h) {
+  return (long long)b * t.sb + (long long)h * t.sh + (long long)pos * t.sl;
+}
+
+template <typename TE>
+__global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_kernel(const NormRopeParams p, const FastDiv fh,
+                                                                   const FastDiv fl) {
+  const int l = threadIdx.x & 7, grp = threadIdx.x >> 3;
+  const long long rows_total = (long long)p.B * p.L * p.H;
+  const NormRopeArgs a{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps};
+  const Frag w = nr_weights(p.w, l);
+  const TE* x = reinterpret_cast<const TE*>(p.x.ptr);
+  TE* y = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
+  for (long long base = (long long)blockIdx.x * kNR64Rows; base < rows_total;
+       base += (long long)gridDim.x * kNR64Rows) {
+    RowWords<TE> in[4];
+    int pos[4];
+    long long yo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const long long row = base + 16 * i + grp;
+      const bool live = row < rows_total;
+      int b, h;
+      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos[i], &h);
+      yo[i] = nr_offset(p.y, b, pos[i], h);
+      in[i] = load_row_words<TE>(x + nr_offset(p.x, b, pos[i], h), 64, l, live);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const Frag z = norm_rope_frag<TE>(FragIO<TE>::from_words(in[i].w), l, w, a, pos[i], p.L, nullptr);
+      if (base + 16 * i + grp < rows_total) store_frag<TE, true>(y + yo[i], 1, 64, l, z);
+    }
+  }
+}
+
+template <typename TE>
+__global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_kernel(const NormRopeParams p, const FastDiv fh,
+                                                                   const FastDiv fl) {
+  __shared__ float sums[16 * 64];
+  const int l = threadIdx.x & 7, grp = threadIdx.x >> 3;
+  const long long rows_total = (long long)p.B * p.L * p.H;
+  const NormRopeArgs a{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps};
+  const Frag w = nr_weights(p.w, l);
+  const TE* x = reinterpret_cast<const TE*>(p.x.ptr);
+  const TE* dy = reinterpret_cast<const TE*>(p.dy.ptr);
+  TE* dx = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
+  Frag dw = frag_zero();
+  for (long long base = (long long)blockIdx.x * kNR64Rows; base < rows_total;
+       base += (long long)gridDim.x * kNR64Rows) {
+    RowWords<TE> xin[4], gin[4];
+    int pos[4];
+    long long xo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const long long row = base + 16 * i + grp;
+      const bool live = row < rows_total;
+      int b, h;
+      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos[i], &h);
+      xo[i] = nr_offset(p.y, b, pos[i], h);
+      xin[i] = load_row_words<TE>(x + nr_offset(p.x, b, pos[i], h), 64, l, live);
+      gin[i] = load_row_words<TE>(dy + nr_offset(p.dy, b, pos[i], h), 64, l, live);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bool live = base + 16 * i + grp < rows_total;
+      const Frag xv = FragIO<TE>::from_words(xin[i].w);
+      const float r = nr_rsqrt(fmaf(nr_row_dot(xv, xv), 1.f / 64.f, p.eps));
+      const Frag g = norm_rope_grad<TE>(FragIO<TE>::from_words(gin[i].w), xv, r, l, w, a, pos[i], p.L, dw, live);
+      if (live) store_frag<TE, true>(dx + xo[i], 1, 64, l, g);
+    }
+  }
+  // Fixed-order column sums of this CTA's row groups -> partial[blockIdx.x][j].
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sums[grp * 64 + 8 * l + 2 * i] = dw.v[i].x;
+    sums[grp * 64 + 8 * l + 2 * i + 1] = dw.v[i].y;
+  }
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float acc = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) acc += sums[g * 64 + threadIdx.x];
+    p.partial[(long long)blockIdx.x * 64 + threadIdx.x] = acc;
+  }
+}
+
+// The vector path's preconditions (host side).
+bool nr_vec_ok(const TensorArg& t, int e) {
+  if (reinterpret_cast<uintptr_t>(t.ptr) % 16 || t.sd != 1) return false;
+  return (t.sb * e) % 16 == 0 && (t.sh * e) % 16 == 0 && (t.sl * e) % 16 == 0;
+}
+
+bool nr_use64(const NormRopeParams& p, int e, bool backward) {
+  if (p.D != 64 || !p.rope) return false;
+  if ((long long)p.B * p.L * p.H >= (1ll << 31)) return false;  // 31-bit row indices (FastDiv)
+  if (reinterpret_cast<uintptr_t>(p.w) % 16 || reinterpret_cast<uintptr_t>(p.cos_t) % 16 ||
+      reinterpret_cast<uintptr_t>(p.sin_t) % 16)
+    return false;
+  return nr_vec_ok(p.x, e) && nr_vec_ok(p.y, e) && (!backward || nr_vec_ok(p.dy, e));
+}
+
 template <typename TE>
 int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
+  if (nr_use64(p, sizeof(TE), false)) {
+    const long long rows = (long long)p.B * p.L * p.H;
+    const long long grid = (rows + kNR64Rows - 1) / kNR64Rows;
+    sbda_norm_rope64_fwd_kernel<TE><<<(unsigned)(grid < (1ll << 20) ? grid : (1ll << 20)), 128, 0, st>>>(
+        p, make_fastdiv((unsigned)p.H), make_fastdiv((unsigned)p.L));
+    return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  }
   const size_t smem = (size_t)kNRRows * (p.D * sizeof(TE) + 4);
   auto kern = sbda_norm_rope_fwd_kernel<TE>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -238,11 +387,18 @@ int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
 
 template <typename TE>
 int nr_backward(const NormRopeParams& p, unsigned blocks, float* grad_w, cudaStream_t st) {
-  const size_t smem = (size_t)kNRRows * (2 * (p.D * sizeof(TE) + 4) + (p.D + 1) * sizeof(float));
-  auto kern = sbda_norm_rope_bwd_kernel<TE>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return SBDA_ERR_CUDA;
-  kern<<<blocks, kNRRows, smem, st>>>(p);
+  if (nr_use64(p, sizeof(TE), true)) {
+    // `blocks` CTAs (at most kNRMaxCtas, device-independent) walk the rows, so
+    // the partials and their summation order do not depend on the GPU.
+    sbda_norm_rope64_bwd_kernel<TE><<<blocks, 128, 0, st>>>(p, make_fastdiv((unsigned)p.H),
+                                                             make_fastdiv((unsigned)p.L));
+  } else {
+    const size_t smem = (size_t)kNRRows * (2 * (p.D * sizeof(TE) + 4) + (p.D + 1) * sizeof(float));
+    auto kern = sbda_norm_rope_bwd_kernel<TE>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return SBDA_ERR_CUDA;
+    kern<<<blocks, kNRRows, smem, st>>>(p);
+  }
   if (cudaGetLastError() != cudaSuccess) return SBDA_ERR_CUDA;
   sbda_norm_weight_reduce_kernel<<<(p.D + 127) / 128, 128, 0, st>>>(p.partial, (int)blocks, p.D, grad_w);
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
