@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("cfg4", "cfg5", "block", "normed"), default="cfg4",
+    p.add_argument("--workload", choices=("cfg4", "cfg5", "block", "normed", "backbone", "gqa"), default="cfg4",
                    help="cfg4 (default, the metric): one 1M-position sequence per GPU; cfg5: one "
                         "4M-position, 22-layer sequence split into contiguous shards across the GPUs")
     p.add_argument("--length", type=int, default=1 << 20)
@@ -387,6 +387,10 @@ def run_b200(args) -> None:
             blocks["cfg4_norm_rope_attention"] = norm_rope_attention_block(device, max(3, min(args.steps, 10)),
                                                                            args.warmup, peak)
             torch.cuda.empty_cache()
+            blocks["cfg4_backbone_vs_dense"] = backbone_block(device, 3, args.warmup)
+            torch.cuda.empty_cache()
+            blocks["gqa"] = gqa_block(device, max(3, min(args.steps, 10)), args.warmup, peak)
+            torch.cuda.empty_cache()
         blocks["cfg3_batch_head"] = cfg3_block(device, world, rank, block_steps, args.warmup, peak, barrier,
                                                max_over_ranks)
         torch.cuda.empty_cache()
@@ -564,6 +568,111 @@ def cfg2_block(device, steps: int, warmup: int, peak: float) -> dict:
                               "frac": (fb + bb) / (step_ms * 1e-3) / 1e9 / peak}},
         "gpu_launches": 2 * steps,
     }
+
+
+def gqa_block(device, steps: int, warmup: int, peak: float, length: int = 1 << 20, layers: int = 20, heads: int = 4,
+              kv_heads: int = 2) -> dict:
+    """Grouped-query attention at the config-4 shape: 4 query heads sharing 2 kv heads, 64 wide,
+    bf16, fwd+bwd of all 20 SBDA layers (``fused_sbda_gqa_key_backward``'s op through the C
+    ABI).  The forward runs on the windowed kernels (K/V rows from kv head h / G); the backward on
+    the general kernels, which sum dK/dV over each group inside the CTA.  Algorithmic bytes per
+    (position, query head) row: Q, dO, O, dQ at 2 * 64 B each way plus K, V, dK, dV once per kv
+    head, and the fp32 LSE written and read."""
+    import sbda_b200
+    from sbda_b200 import ops
+
+    D = 64
+    offsets = sbda_b200.sbda_layer_offsets(layers)
+    gen = torch.Generator(device=device).manual_seed(9)
+    qs = [_blhd((1, length, heads, D), device, gen) for _ in range(layers)]
+    dos = [_blhd((1, length, heads, D), device, gen) for _ in range(layers)]
+    ks = [_blhd((1, length, kv_heads, D), device, gen) for _ in range(layers)]
+    vs = [_blhd((1, length, kv_heads, D), device, gen) for _ in range(layers)]
+    lses = [torch.empty((1, heads, length), device=device, dtype=torch.float32) for _ in range(layers)]
+    out = torch.empty_like(qs[0])
+    grads = (torch.empty_like(qs[0]), torch.empty_like(ks[0]), torch.empty_like(vs[0]))
+
+    def fwd():
+        for layer in range(layers):
+            ops.sbda_forward(qs[layer], ks[layer], vs[layer], offsets[layer], out=out, lse=lses[layer])
+
+    def bwd():
+        for layer in reversed(range(layers)):
+            ops.sbda_backward(qs[layer], ks[layer], vs[layer], dos[layer], lses[layer], offsets[layer], grads=grads)
+
+    fwd_ms = timed_steps(fwd, steps, warmup, None)
+    bwd_ms = timed_steps(bwd, steps, warmup, None)
+    e = 2
+    q_rows, kv_rows = length * heads * layers, length * kv_heads * layers
+    fwd_bytes = q_rows * (2 * D * e + 4) + kv_rows * 2 * D * e
+    bwd_bytes = q_rows * (4 * D * e + 4) + kv_rows * 4 * D * e
+    return {
+        "workload": (f"GQA: {length} positions x {layers} layers, {heads} query heads / {kv_heads} kv heads x {D}, "
+                     "bf16, fwd+bwd"),
+        "value": length / ((fwd_ms + bwd_ms) * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": fwd_ms + bwd_ms,
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "kernels": "forward: windowed kernels; backward: general kernels (in-CTA group sum of dK/dV)",
+        "l2": "every q/dO tensor 512 MiB, k/v 256 MiB > 126 MB L2",
+        "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s",
+                     "fwd_frac": fwd_bytes / (fwd_ms * 1e-3) / 1e9 / peak,
+                     "bwd_frac": bwd_bytes / (bwd_ms * 1e-3) / 1e9 / peak},
+        "gpu_launches": 2 * layers * steps,
+    }
+
+
+def backbone_block(device, steps: int, warmup: int, length: int = 1 << 20, layers: int = 20, dim: int = 256,
+                   heads: int = 4, ffn: int = 1024) -> dict:
+    """Config 4's forward comparison, as the reference's protocol runs it
+    (``BinaryDiffusionAttention/bench_gemm_breakdown.py:120-209``: ``forward_hidden`` of a
+    ``BiAttnLM``, no vocabulary head, bf16, batch 1).  The shape is config 4's: 1,048,576 positions,
+    20 layers, d_model 256, 4 heads x 64, FFN 1024.  Timed on the same GPU:
+
+    * the whole backbone forward (``sbda_b200.BiAttnLM`` in bf16: norms, projections, SBDA
+      attention, SwiGLU FFN);
+    * the 20 SBDA attention forwards alone (the C-ABI op on q/k/v of this shape);
+    * dense causal attention: torch's scaled_dot_product_attention(is_causal=True) on the same
+      q/k/v.  It is timed on one layer, since its cost does not depend on the layer, and counted
+      20 times.  The dense backbone is the SBDA backbone with the SBDA attention time replaced by
+      the dense one.
+    """
+    import torch.nn.functional as F
+
+    import sbda_b200
+    from sbda_b200 import ops
+
+    torch.manual_seed(1)
+    cfg = sbda_b200.BiAttnConfig(vocab_size=6400, dim=dim, layers=layers, heads=heads, ff_hidden=ffn,
+                                 attention_backend="sbda")
+    model = sbda_b200.BiAttnLM(cfg).to(device=device, dtype=torch.bfloat16).eval()
+    gen = torch.Generator(device=device).manual_seed(5)
+    ids = torch.randint(6400, (1, length), device=device, generator=gen)
+    head_dim = dim // heads
+    q, k, v = (_blhd((1, length, heads, head_dim), device, gen) for _ in range(3))
+    out, lse = torch.empty_like(q), torch.empty((1, heads, length), device=device, dtype=torch.float32)
+    offsets = sbda_b200.sbda_layer_offsets(layers)
+    result = {"workload": (f"cfg4 forward: BiAttnLM.forward_hidden, {length} positions x {layers} layers, d_model {dim}, "
+                           f"{heads} heads x {head_dim}, FFN {ffn}, bf16, batch 1 (no vocabulary head)"),
+              "unit": "ms"}
+    with torch.inference_mode():
+        result["backbone_fwd_ms"] = timed_steps(lambda: model.forward_hidden(ids), steps, warmup, None)
+        result["sbda_attention_fwd_ms"] = timed_steps(
+            lambda: [ops.sbda_forward(q, k, v, offsets[layer], out=out, lse=lse) for layer in range(layers)],
+            steps, warmup, None)
+        del model
+        torch.cuda.empty_cache()
+        try:
+            dense_layer = timed_steps(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), 2, 1, None)
+            result["dense_attention_fwd_ms"] = dense_layer * layers
+            result["dense_attention_fwd_ms_one_layer"] = dense_layer
+            result["dense_backbone_fwd_ms"] = (result["backbone_fwd_ms"] - result["sbda_attention_fwd_ms"]
+                                               + result["dense_attention_fwd_ms"])
+            result["attention_speedup_vs_dense"] = result["dense_attention_fwd_ms"] / result["sbda_attention_fwd_ms"]
+            result["backbone_speedup_vs_dense"] = result["dense_backbone_fwd_ms"] / result["backbone_fwd_ms"]
+        except (RuntimeError, torch.OutOfMemoryError) as err:  # reported, not fatal for the bench line
+            result["dense_attention_error"] = str(err).splitlines()[0][:200]
+    result["value"] = length / (result["backbone_fwd_ms"] * 1e-3) / 1e6
+    result["value_unit"] = "Mpositions/s (backbone forward)"
+    return result
 
 
 def norm_rope_attention_block(device, steps: int, warmup: int, peak: float, length: int = 1 << 20, heads: int = 4,
@@ -848,6 +957,15 @@ def main() -> None:
         run_seqshard(args)
     elif args.workload == "block":
         run_block(args)
+    elif args.workload == "gqa":
+        torch.cuda.set_device(0)
+        peak, _ = measured_peak_gbs()
+        print(json.dumps(gqa_block(torch.device("cuda", 0), args.steps, args.warmup, peak, length=args.length,
+                                   layers=args.layers)), flush=True)
+    elif args.workload == "backbone":
+        torch.cuda.set_device(0)
+        print(json.dumps(backbone_block(torch.device("cuda", 0), args.steps, args.warmup, length=args.length,
+                                        layers=args.layers)), flush=True)
     elif args.workload == "normed":
         torch.cuda.set_device(0)
         peak, _ = measured_peak_gbs()

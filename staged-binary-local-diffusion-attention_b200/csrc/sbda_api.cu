@@ -533,9 +533,12 @@ extern "C" int sbda_b200_forward_ex(int family, int dtype, sbda_shape shape, con
   const bool vec = tensors_vector_ok({&q, &k, &v, &out}, B, L, D, e, {H, Hkv, Hkv, H});
 
   V2Plan p2;
-  if (family == kFamilyAuto && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
+  // The windowed forward serves grouped-query attention too (K/V rows from kv head h / G); its
+  // plan does not depend on G, so it is made as for MHA.
+  if (family == kFamilyAuto && plan_v2(offsets, n_offsets, L, D, e, 1, B, H, &p2)) {
     FwdV2Params p;
     memset(&p, 0, sizeof(p));
+    p.G = (int)(H / Hkv);
     p.B = (int)B;
     p.H = (int)H;
     p.L = (int)L;
@@ -555,10 +558,10 @@ extern "C" int sbda_b200_forward_ex(int family, int dtype, sbda_shape shape, con
     if (tma) {
       unsigned dummy;
       tma = encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p2.pitch, p2.tile) &&
-            encode_map(&maps.kT, &p.slots_k, k, dtype, B, H, L, D, p2.pitch, p2.tile) &&
-            encode_map(&maps.vT, &p.slots_v, v, dtype, B, H, L, D, p2.pitch, p2.tile) &&
-            encode_map(&maps.kH, &dummy, k, dtype, B, H, L, D, p2.pitch, fwd_window_lead(p2.g, p2.tile)) &&
-            encode_map(&maps.vH, &dummy, v, dtype, B, H, L, D, p2.pitch, fwd_window_lead(p2.g, p2.tile));
+            encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p2.pitch, p2.tile) &&
+            encode_map(&maps.kH, &dummy, k, dtype, B, Hkv, L, D, p2.pitch, fwd_window_lead(p2.g, p2.tile)) &&
+            encode_map(&maps.vH, &dummy, v, dtype, B, Hkv, L, D, p2.pitch, fwd_window_lead(p2.g, p2.tile));
     }
     return v2_forward(dtype, tma, maps, p, p2, s);
   }
@@ -837,6 +840,7 @@ extern "C" int sbda_b200_forward_sharded_ex(int family, int dtype, sbda_shape sh
         Ls % p2.tile == 0 && vector_ok(q, B, H, Ls, D, e) && vector_ok(out, B, H, Ls, D, e)) {
       FwdV2Params p;
       memset(&p, 0, sizeof(p));
+      p.G = 1;
       p.B = (int)B;
       p.H = (int)H;
       p.L = (int)Ls;
@@ -1082,6 +1086,7 @@ extern "C" int sbda_b200_forward_normed(int dtype, sbda_shape shape, const int32
   if (!q_raw.data || !k_raw.data || !v.data || !out.data || !lse) return SBDA_ERR_INVALID;
   FwdV2Params p;
   memset(&p, 0, sizeof(p));
+  p.G = 1;
   if ((st = normed_args(&p.nq, q_weight, q_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
   if ((st = normed_args(&p.nk, k_weight, k_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
   const int e = elem_size(dtype);

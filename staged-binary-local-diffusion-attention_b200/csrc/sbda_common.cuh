@@ -603,6 +603,7 @@ struct NormRopeArgs {
 
 struct FwdV2Params {
   int B, H, L, D;        // L: positions of this call's rows (the shard when sharded)
+  int G;                 // query heads per kv head (1 = MHA); K/V rows come from kv head h / G
   float scale;
   V2Geometry g;
   TensorArg q, k, v, out;

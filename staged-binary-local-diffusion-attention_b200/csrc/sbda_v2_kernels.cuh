@@ -312,6 +312,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   const int t = chain_tile_v2(bid % g.nT, g.R, g.A, g.rem);
   const int b = bid / g.nT;
   const int i0 = t * T;
+  const int hk = h / p.G;  // kv head of query head h (grouped-query attention; G = 1 for MHA)
   const bool has1 = SHAPE == 0 ? g.has1 != 0 : (SHAPE == 1 || SHAPE >= 3);
   const bool has2 = SHAPE == 0 ? g.has2 != 0 : SHAPE >= 2;
   const bool far = SHAPE == 0 ? g.has_far != 0 : SHAPE >= 3;
@@ -345,13 +346,13 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
       const int ig = p.sh.pos0 + i0;
       int c;
       mbar_arrive_expect_tx(bar, (uint32_t)((2 * (T + lead) + (far && !near_far ? 2 * T : 0)) * P));
-      tma_rows(Kn, pick_map(maps.kH, p.sh, ig - lead, c), bar, p.slots_k, c, h, b);
-      tma_rows(Vn, pick_map(maps.vH, p.sh, ig - lead, c), bar, p.slots_v, c, h, b);
-      tma_rows(Kn + lead * P, pick_map(maps.kT, p.sh, ig, c), bar, p.slots_k, c, h, b);
-      tma_rows(Vn + lead * P, pick_map(maps.vT, p.sh, ig, c), bar, p.slots_v, c, h, b);
+      tma_rows(Kn, pick_map(maps.kH, p.sh, ig - lead, c), bar, p.slots_k, c, hk, b);
+      tma_rows(Vn, pick_map(maps.vH, p.sh, ig - lead, c), bar, p.slots_v, c, hk, b);
+      tma_rows(Kn + lead * P, pick_map(maps.kT, p.sh, ig, c), bar, p.slots_k, c, hk, b);
+      tma_rows(Vn + lead * P, pick_map(maps.vT, p.sh, ig, c), bar, p.slots_v, c, hk, b);
       if (far && !near_far) {
-        tma_rows(Kf, pick_map(maps.kT, p.sh, ig - g.d, c), bar, p.slots_k, c, h, b);
-        tma_rows(Vf, pick_map(maps.vT, p.sh, ig - g.d, c), bar, p.slots_v, c, h, b);
+        tma_rows(Kf, pick_map(maps.kT, p.sh, ig - g.d, c), bar, p.slots_k, c, hk, b);
+        tma_rows(Vf, pick_map(maps.vT, p.sh, ig - g.d, c), bar, p.slots_v, c, hk, b);
       }
     }
     // Q rows of this group, in flight while the K/V copies land.
@@ -376,11 +377,11 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
   } else {
     constexpr int PE = P / sizeof(TE);
     generic_rows<TE>(Qs, p.q, b, h, i0, T, p.L, p.D, PE);
-    generic_rows<TE>(Kn, p.k, b, h, i0 - lead, T + lead, p.L, p.D, PE);
-    generic_rows<TE>(Vn, p.v, b, h, i0 - lead, T + lead, p.L, p.D, PE);
+    generic_rows<TE>(Kn, p.k, b, hk, i0 - lead, T + lead, p.L, p.D, PE);
+    generic_rows<TE>(Vn, p.v, b, hk, i0 - lead, T + lead, p.L, p.D, PE);
     if (far && !near_far) {
-      generic_rows<TE>(Kf, p.k, b, h, i0 - g.d, T, p.L, p.D, PE);
-      generic_rows<TE>(Vf, p.v, b, h, i0 - g.d, T, p.L, p.D, PE);
+      generic_rows<TE>(Kf, p.k, b, hk, i0 - g.d, T, p.L, p.D, PE);
+      generic_rows<TE>(Vf, p.v, b, hk, i0 - g.d, T, p.L, p.D, PE);
     }
     __syncthreads();
   }
