@@ -18,7 +18,7 @@
 // row pitch of D*e + 4 bytes (an odd number of words for even D), so the
 // lanes of a warp, reading the same channel of 32 consecutive rows, hit
 // distinct banks.  Staging loads/stores are warp-per-row and coalesced.
-// The backward is a fixed-size grid (at most kNRMaxCtas CTAs, independent
+// The backward is a fixed-size grid (at most 2048 / 1024 CTAs, independent
 // of the device) walking row blocks; each CTA keeps its weight-gradient
 // column sums and writes them once, so the final reduction is short and
 // its order is fixed.
@@ -30,7 +30,7 @@
 namespace sbda {
 
 constexpr int kNRRows = 128;      // rows per CTA step (one per thread)
-constexpr int kNRMaxCtas = 1024;  // backward grid cap (partials per weight vector)
+constexpr int kNRMaxCtas = 1024;  // backward grid cap for head_dim > 64 (twice this at <= 64)
 
 struct NormRopeParams {
   int B, L, H, D;
@@ -216,14 +216,28 @@ __global__ void __launch_bounds__(kNRRows) sbda_norm_rope_bwd_kernel(const NormR
   }
 }
 
-// dw[j] = sum over blocks (fixed order) of partial[block][j].
-__global__ void sbda_norm_weight_reduce_kernel(const float* __restrict__ partial, int blocks, int D,
-                                               float* __restrict__ dw) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= D) return;
+// dw[j] = sum over blocks of partial[block][j] in a fixed order: thread (j, s)
+// sums slice s of blockDim.y consecutive row ranges in row order, then the
+// slice sums are added in slice order.  The slice count depends on D only, so
+// the order is independent of timing and device: deterministic.
+constexpr int kDwMaxSlices = 16;
+
+__global__ void __launch_bounds__(1024) sbda_norm_weight_reduce_kernel(const float* __restrict__ partial,
+                                                                       int blocks, int D, float* __restrict__ dw) {
+  __shared__ float slice_sum[kDwMaxSlices][128];
+  const int j = threadIdx.x, sl = threadIdx.y, slices = blockDim.y;
+  const int per = (blocks + slices - 1) / slices;
+  const int lo = sl * per, hi = min(blocks, lo + per);
   float acc = 0.f;
-  for (int b = 0; b < blocks; ++b) acc += partial[(long long)b * D + j];
-  dw[j] = acc;
+#pragma unroll 8
+  for (int b = lo; b < hi; ++b) acc += partial[(long long)b * D + j];
+  slice_sum[sl][j] = acc;
+  __syncthreads();
+  if (sl == 0) {
+    float total = 0.f;
+    for (int t = 0; t < slices; ++t) total += slice_sum[t][j];
+    dw[j] = total;
+  }
 }
 
 // --------------------------------------------------------------------------
@@ -302,40 +316,57 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_kernel(const NormRop
   }
 }
 
+// One CTA iteration's input rows of the backward: x and dy of 4 rows per lane.
+template <typename TE>
+struct NR64BwdRows {
+  RowWords<TE> x[4], g[4];
+  int pos[4];
+  long long dxo[4];
+};
+
+template <typename TE>
+__device__ __forceinline__ void nr64_bwd_load(NR64BwdRows<TE>& r, const NormRopeParams& p, long long base,
+                                              long long rows_total, int grp, int l, const FastDiv& fh,
+                                              const FastDiv& fl) {
+  const TE* x = reinterpret_cast<const TE*>(p.x.ptr);
+  const TE* dy = reinterpret_cast<const TE*>(p.dy.ptr);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const long long row = base + 16 * i + grp;
+    const bool live = row < rows_total;
+    int b, h;
+    nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &r.pos[i], &h);
+    r.dxo[i] = nr_offset(p.y, b, r.pos[i], h);
+    r.x[i] = load_row_words<TE>(x + nr_offset(p.x, b, r.pos[i], h), 64, l, live);
+    r.g[i] = load_row_words<TE>(dy + nr_offset(p.dy, b, r.pos[i], h), 64, l, live);
+  }
+}
+
+// Loads of an iteration are issued together (8 per lane), then its math runs.
+// (Loading the next iteration's rows during this one's math needs ~160
+// registers: 3 CTAs per SM instead of 4, and measured 22 % slower.)
 template <typename TE>
 __global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_kernel(const NormRopeParams p, const FastDiv fh,
                                                                    const FastDiv fl) {
   __shared__ float sums[16 * 64];
   const int l = threadIdx.x & 7, grp = threadIdx.x >> 3;
   const long long rows_total = (long long)p.B * p.L * p.H;
+  const long long stride = (long long)gridDim.x * kNR64Rows;
   const NormRopeArgs a{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps};
   const Frag w = nr_weights(p.w, l);
-  const TE* x = reinterpret_cast<const TE*>(p.x.ptr);
-  const TE* dy = reinterpret_cast<const TE*>(p.dy.ptr);
   TE* dx = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
   Frag dw = frag_zero();
-  for (long long base = (long long)blockIdx.x * kNR64Rows; base < rows_total;
-       base += (long long)gridDim.x * kNR64Rows) {
-    RowWords<TE> xin[4], gin[4];
-    int pos[4];
-    long long xo[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const long long row = base + 16 * i + grp;
-      const bool live = row < rows_total;
-      int b, h;
-      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos[i], &h);
-      xo[i] = nr_offset(p.y, b, pos[i], h);
-      xin[i] = load_row_words<TE>(x + nr_offset(p.x, b, pos[i], h), 64, l, live);
-      gin[i] = load_row_words<TE>(dy + nr_offset(p.dy, b, pos[i], h), 64, l, live);
-    }
+  for (long long base = (long long)blockIdx.x * kNR64Rows; base < rows_total; base += stride) {
+    NR64BwdRows<TE> cur;
+    nr64_bwd_load(cur, p, base, rows_total, grp, l, fh, fl);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const bool live = base + 16 * i + grp < rows_total;
-      const Frag xv = FragIO<TE>::from_words(xin[i].w);
+      const Frag xv = FragIO<TE>::from_words(cur.x[i].w);
       const float r = nr_rsqrt(fmaf(nr_row_dot(xv, xv), 1.f / 64.f, p.eps));
-      const Frag g = norm_rope_grad<TE>(FragIO<TE>::from_words(gin[i].w), xv, r, l, w, a, pos[i], p.L, dw, live);
-      if (live) store_frag<TE, true>(dx + xo[i], 1, 64, l, g);
+      const Frag g =
+          norm_rope_grad<TE>(FragIO<TE>::from_words(cur.g[i].w), xv, r, l, w, a, cur.pos[i], p.L, dw, live);
+      if (live) store_frag<TE, true>(dx + cur.dxo[i], 1, 64, l, g);
     }
   }
   // Fixed-order column sums of this CTA's row groups -> partial[blockIdx.x][j].
@@ -388,7 +419,7 @@ int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
 template <typename TE>
 int nr_backward(const NormRopeParams& p, unsigned blocks, float* grad_w, cudaStream_t st) {
   if (nr_use64(p, sizeof(TE), true)) {
-    // `blocks` CTAs (at most kNRMaxCtas, device-independent) walk the rows, so
+    // `blocks` CTAs (a cap that depends on head_dim only, not the device) walk the rows, so
     // the partials and their summation order do not depend on the GPU.
     sbda_norm_rope64_bwd_kernel<TE><<<blocks, 128, 0, st>>>(p, make_fastdiv((unsigned)p.H),
                                                              make_fastdiv((unsigned)p.L));
@@ -400,7 +431,8 @@ int nr_backward(const NormRopeParams& p, unsigned blocks, float* grad_w, cudaStr
     kern<<<blocks, kNRRows, smem, st>>>(p);
   }
   if (cudaGetLastError() != cudaSuccess) return SBDA_ERR_CUDA;
-  sbda_norm_weight_reduce_kernel<<<(p.D + 127) / 128, 128, 0, st>>>(p.partial, (int)blocks, p.D, grad_w);
+  const int slices = p.D <= 64 ? kDwMaxSlices : kDwMaxSlices / 2;  // D * slices <= 1024 threads
+  sbda_norm_weight_reduce_kernel<<<1, dim3(p.D, slices), 0, st>>>(p.partial, (int)blocks, p.D, grad_w);
   return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
@@ -409,11 +441,14 @@ int64_t norm_rope_blocks(const sbda_shape& s) {
   return (rows + kNRRows - 1) / kNRRows;
 }
 
-// Backward grid: one CTA per row block up to kNRMaxCtas (device-independent,
-// so the weight-gradient summation order is too).
+// Backward grid: one CTA per row block up to a cap that depends only on the
+// head size (device-independent, so the weight-gradient summation order is
+// too): 2 * kNRMaxCtas for head_dim <= 64, kNRMaxCtas above.  Either way the
+// partials fit in kNRMaxCtas * 128 floats.
 int64_t norm_rope_bwd_ctas(const sbda_shape& s) {
   const int64_t b = norm_rope_blocks(s);
-  return b < kNRMaxCtas ? b : kNRMaxCtas;
+  const int64_t cap = s.head_dim <= 64 ? 2 * kNRMaxCtas : kNRMaxCtas;
+  return b < cap ? b : cap;
 }
 
 int norm_rope_check(int dtype, const sbda_shape& s, float eps) {
@@ -502,7 +537,8 @@ extern "C" int sbda_b200_norm_rope_backward(int dtype, sbda_shape shape, sbda_te
 // plugin hosts that forbid allocation in the execution callback.  For them
 // the weight-gradient partials live in this file-scope array instead of a
 // caller workspace.  It holds kNoAllocScratchFloats floats (512 KiB: 1024
-// CTAs x 128 channels, enough for every shape the backward accepts) on every
+// CTAs x 128 channels, or 2048 CTAs x 64 channels at head_dim <= 64; enough for
+// every shape the backward accepts) on every
 // GPU that loads the library, until the process exits.
 //
 // Every call shares the array.  Each CTA overwrites its partial row before

@@ -147,7 +147,10 @@ def test_norm_rope_validation_codes(lib):
     assert fwd(2, _lib.SbdaShape(1, 4, 4, 0, 64), t, t, 16, 1e-6, 16, 16, 0, None) == _lib.SBDA_OK
     # one partial row of fp32 per CTA of 128 rows, capped at 1024 CTAs
     assert lib.sbda_b200_norm_rope_workspace_floats(s) == 32 * 64
-    assert lib.sbda_b200_norm_rope_workspace_floats(_lib.SbdaShape(8, 8, 8, 1 << 20, 64)) == 1024 * 64
+    # Backward grid cap: 2048 CTAs at head_dim <= 64, 1024 above; the partials always fit the
+    # allocation-free entry point's 1024 x 128-float array.
+    assert lib.sbda_b200_norm_rope_workspace_floats(_lib.SbdaShape(8, 8, 8, 1 << 20, 64)) == 2048 * 64
+    assert lib.sbda_b200_norm_rope_workspace_floats(_lib.SbdaShape(8, 8, 8, 1 << 20, 128)) == 1024 * 128
     bwd = lib.sbda_b200_norm_rope_backward
     assert bwd(2, s, t, t, 16, 1e-6, 16, 16, 0, t, 16, 16, 2047, None) == _lib.SBDA_ERR_INVALID  # workspace
     assert bwd(2, s, t, t, 16, 1e-6, 16, 16, 0, t, None, 16, 2048, None) == _lib.SBDA_ERR_INVALID
