@@ -61,7 +61,7 @@ def parse_args():
                    help="comma-separated subset of layers to run (profiling cases); default all")
     p.add_argument("--heads", type=int, default=4)
     p.add_argument("--head-dim", type=int, default=64)
-    p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-blocks", action="store_true",
@@ -340,6 +340,46 @@ def run_b200(args) -> None:
     clocks = sampler.stop()
     step_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
 
+    # Host time to issue one step's 40 launches (no synchronisation inside), median of 3.
+    host_ms = []
+    for _ in range(3):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        step()
+        host_ms.append((time.perf_counter() - t0) * 1e3)
+    torch.cuda.synchronize()
+    host_ms = statistics.median(host_ms)
+
+    # The same step captured once as a CUDA graph and replayed: the same 40 kernels on the same
+    # buffers, without the per-launch host work (planning, tensor-map encoding, ctypes calls).
+    graph_info = None
+    try:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        barrier()
+        torch.cuda.synchronize()
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gs.record()
+        for _ in range(args.steps):
+            graph.replay()
+        ge.record()
+        torch.cuda.synchronize()
+        barrier()
+        graph_ms = max_over_ranks(gs.elapsed_time(ge) / args.steps)
+        graph_info = {"ms_per_step": graph_ms, "value": L * world / (graph_ms * 1e-3) / 1e6, "unit": UNIT}
+        del graph
+    except RuntimeError as err:  # reported, not fatal for the bench line
+        graph_info = {"error": str(err).splitlines()[0][:200]}
+
     # Per-kernel durations (separate pass with an event pair around every launch).
     for _ in range(2):
         step(record=True)
@@ -412,7 +452,14 @@ def run_b200(args) -> None:
                               "algorithmic_bytes_per_step": step_bytes, "fwd_launch_ms": fwd_ms,
                               "bwd_launch_ms": bwd_ms,
                               "fwd_layer_ms": [round(x, 4) for x in fwd_layer_ms],
-                              "bwd_layer_ms": [round(x, 4) for x in bwd_layer_ms]},
+                              "bwd_layer_ms": [round(x, 4) for x in bwd_layer_ms],
+                              "sum_launch_ms": layers * (fwd_ms + bwd_ms),
+                              "gap_ms": step_ms - layers * (fwd_ms + bwd_ms),
+                              "gap_note": ("step time minus the per-launch event times; an event pair around "
+                                           "every launch serialises the kernels, so the sum can exceed the "
+                                           "back-to-back step and the gap be negative"),
+                              "host_enqueue_ms_per_step": host_ms},
+            "graph_replay": graph_info,
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -485,17 +532,19 @@ def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
     steps = max(1, args.e2e_steps)
     barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    marks[0].record()
+    for i in range(steps):
         step()
-    end.record()
+        marks[i + 1].record()
     torch.cuda.synchronize()
     barrier()
-    ms = max_over_ranks(start.elapsed_time(end) / steps)
+    per_step = [marks[i].elapsed_time(marks[i + 1]) for i in range(steps)]
+    ms = max_over_ranks(marks[0].elapsed_time(marks[-1]) / steps)
     tensor_bytes = L * H * D * 2
     return {"value": L * world / (ms * 1e-3) / 1e6, "unit": UNIT, "h2d_bytes_per_step": 4 * tensor_bytes * layers,
             "d2h_bytes_per_step": 3 * tensor_bytes * layers, "ms_per_step": ms, "steps": steps,
+            "ms_per_step_min_max": [min(per_step), max(per_step)],
             "api": "sbda_b200.fused_sbda_key_backward + autograd backward, pinned host buffers; "
                    "copies on two side streams overlapped with compute"}
 

@@ -4,8 +4,10 @@
 #include "sbda_common.cuh"
 
 #include <atomic>
+#include <map>
 #include <mutex>
 #include <string.h>
+#include <tuple>
 
 namespace sbda {
 
@@ -32,10 +34,18 @@ unsigned* status_ptr() {
 constexpr int kFamilyAuto = 0, kFamilyGeneral = 1, kFamilyUniform = 2;
 bool family_ok(int family) { return family >= kFamilyAuto && family <= kFamilyUniform; }
 
+// SM count of the current device, read once per device.
 int sm_count() {
+  static std::atomic<int> cache[64];
   int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  if (cudaGetDevice(&dev) != cudaSuccess) return n;
+  if (dev >= 0 && dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
 }
 
 // --------------------------------------------------------------------------
@@ -294,6 +304,24 @@ int balanced_segment(int64_t chains, int len, bool pre, int64_t slots) {
   return best;
 }
 
+// balanced_segment searches up to 8192 splits; a layer calls it with the same
+// arguments every step, so results are kept (a few hundred entries at most).
+int balanced_segment_cached(int64_t chains, int len, bool pre, int64_t slots) {
+  static std::mutex mu;
+  static std::map<std::tuple<int64_t, int, bool, int64_t>, int> cache;
+  const auto key = std::make_tuple(chains, len, pre, slots);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int seg = balanced_segment(chains, len, pre, slots);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 512) cache.clear();
+  cache.emplace(key, seg);
+  return seg;
+}
+
 // L: rows of this call (a shard when sequence-sharded); total_L: positions of
 // the whole sequence (offsets at or beyond it never have a source).
 bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, int64_t B, int64_t H,
@@ -358,7 +386,7 @@ bool plan_v2(const int32_t* off, int n, int64_t L, int64_t D, int e, int64_t G, 
   // one CTA each.
   const int64_t chains = g.mode == 0 ? B * H * (int64_t)g.chains : B * H;
   const int len = g.mode == 0 ? g.A : g.nT;
-  g.seg = balanced_segment(chains, len, g.mode != 1, (int64_t)sm_count() * 3);
+  g.seg = balanced_segment_cached(chains, len, g.mode != 1, (int64_t)sm_count() * 3);
   g.segs = (len + g.seg - 1) / g.seg;
   pl->blocks_bwd = (unsigned)(chains * g.segs);
   pl->g = g;
