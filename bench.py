@@ -623,10 +623,12 @@ def gqa_block(device, steps: int, warmup: int, peak: float, length: int = 1 << 2
               kv_heads: int = 2) -> dict:
     """Grouped-query attention at the config-4 shape: 4 query heads sharing 2 kv heads, 64 wide,
     bf16, fwd+bwd of all 20 SBDA layers (``fused_sbda_gqa_key_backward``'s op through the C
-    ABI).  The forward runs on the windowed kernels (K/V rows from kv head h / G); the backward on
-    the general kernels, which sum dK/dV over each group inside the CTA.  Algorithmic bytes per
-    (position, query head) row: Q, dO, O, dQ at 2 * 64 B each way plus K, V, dK, dV once per kv
-    head, and the fp32 LSE written and read."""
+    ABI).  Both directions run on the windowed kernels with K/V rows from kv head h / G; the
+    backward writes fp32 per-query-head dK/dV partials to a workspace and sums each group in a
+    fixed order (``sbda_b200_backward_grouped``).  Algorithmic bytes per (position, query head)
+    row: Q, dO, O, dQ at 2 * 64 B each plus K, V, dK, dV once per kv head, and the fp32 LSE written
+    and read; the partials' round trip (2 x 4 x 64 B written and read per query row) is not
+    algorithmic and counts against the fraction."""
     import sbda_b200
     from sbda_b200 import ops
 
@@ -660,7 +662,8 @@ def gqa_block(device, steps: int, warmup: int, peak: float, length: int = 1 << 2
                      "bf16, fwd+bwd"),
         "value": length / ((fwd_ms + bwd_ms) * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": fwd_ms + bwd_ms,
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-        "kernels": "forward: windowed kernels; backward: general kernels (in-CTA group sum of dK/dV)",
+        "kernels": ("windowed kernels both ways (K/V from kv head h / G); backward: fp32 per-query-head dK/dV "
+                    "partials, then a fixed-order group sum"),
         "l2": "every q/dO tensor 512 MiB, k/v 256 MiB > 126 MB L2",
         "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s",
                      "fwd_frac": fwd_bytes / (fwd_ms * 1e-3) / 1e9 / peak,

@@ -110,6 +110,23 @@ int sbda_b200_backward(int dtype, sbda_shape shape, const int32_t* offsets, int3
                        void* stream);
 
 /*
+ * Backward for grouped-query attention (kv_heads < heads) on the windowed
+ * kernels.  Replaces _FusedSBDAGQAKeyBackward.backward (sbda_triton.py:1402-1434),
+ * which sums dK/dV over each group with atomics.  Here every query head writes
+ * its dK/dV contributions as fp32 partials to `workspace` (at least
+ * sbda_b200_backward_grouped_workspace_floats(shape) floats, 16-byte aligned),
+ * and a second kernel sums the partials of each kv head in head order and
+ * rounds once: deterministic.  Calls the windowed kernels do not serve (and MHA
+ * calls) run sbda_b200_backward, which ignores the workspace.
+ */
+int64_t sbda_b200_backward_grouped_workspace_floats(sbda_shape shape);
+int sbda_b200_backward_grouped(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                               float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                               sbda_tensor grad_out, const float* lse, sbda_tensor grad_q,
+                               sbda_tensor grad_k, sbda_tensor grad_v, float* workspace,
+                               int64_t workspace_floats, void* stream);
+
+/*
  * Contiguous sequence shards (no counterpart in the reference, which runs
  * one sequence on one GPU).  Rank r of `world` (<= 8) holds
  * positions [r*L, (r+1)*L) of one sequence, L = shape.length, the same on

@@ -175,6 +175,11 @@ def load() -> ctypes.CDLL:
             c_void_p, c_float, c_void_p, c_float, c_void_p, c_void_p, ctypes.c_int64, SbdaTensor, SbdaTensor,
             SbdaTensor, c_void_p, c_void_p, c_void_p, ctypes.c_int64, c_void_p,
         ]
+        lib.sbda_b200_backward_grouped_workspace_floats.restype = ctypes.c_int64
+        lib.sbda_b200_backward_grouped_workspace_floats.argtypes = [SbdaShape]
+        lib.sbda_b200_backward_grouped.restype = c_int
+        lib.sbda_b200_backward_grouped.argtypes = list(lib.sbda_b200_backward.argtypes[:-1]) + [
+            c_void_p, ctypes.c_int64, c_void_p]
         fwd_args = lib.sbda_b200_forward.argtypes
         bwd_args = lib.sbda_b200_backward.argtypes
         lib.sbda_b200_forward_ex.restype = c_int

@@ -658,6 +658,7 @@ extern "C" int sbda_b200_backward_ex(int family, int dtype, sbda_shape shape, co
   if (family == kFamilyAuto && plan_v2(offsets, n_offsets, L, D, e, H / Hkv, B, H, &p2)) {
     BwdV2Params p;
     memset(&p, 0, sizeof(p));
+    p.G = 1;
     p.B = (int)B;
     p.H = (int)H;
     p.L = (int)L;
@@ -957,6 +958,7 @@ extern "C" int sbda_b200_backward_sharded_ex(int family, int dtype, sbda_shape s
         vector_ok(grad_v, B, H, Ls, D, e)) {
       BwdV2Params p;
       memset(&p, 0, sizeof(p));
+      p.G = 1;
       p.B = (int)B;
       p.H = (int)H;
       p.L = (int)Ls;
@@ -1179,6 +1181,7 @@ extern "C" int sbda_b200_backward_normed(int dtype, sbda_shape shape, const int3
   if (workspace_floats < v2_normed_workspace_floats(p2.blocks_bwd)) return SBDA_ERR_INVALID;
   BwdV2Params p;
   memset(&p, 0, sizeof(p));
+  p.G = 1;
   if ((st = normed_args(&p.nq, q_weight, q_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
   if ((st = normed_args(&p.nk, k_weight, k_eps, cos_table, sin_table, table_offset)) != SBDA_OK) return st;
   const int e = elem_size(dtype);
@@ -1220,4 +1223,81 @@ extern "C" int sbda_b200_backward_normed(int dtype, sbda_shape shape, const int3
     return SBDA_ERR_UNSUPPORTED;
   p.lse_tma = encode_lse_map(&maps.lseT, lse, B * H, L, p2.lse_box);
   return v2_backward_normed(dtype, maps, p, p2, grad_q_weight, grad_k_weight, workspace, s);
+}
+
+// --------------------------------------------------------------------------
+// Grouped-query attention on the windowed backward
+// --------------------------------------------------------------------------
+
+extern "C" int64_t sbda_b200_backward_grouped_workspace_floats(sbda_shape shape) {
+  if (shape.batch < 0 || shape.heads < 0 || shape.length < 0 || shape.head_dim < 1) return -1;
+  return 2 * shape.batch * shape.heads * shape.length * shape.head_dim;
+}
+
+extern "C" int sbda_b200_backward_grouped(int dtype, sbda_shape shape, const int32_t* offsets, int32_t n_offsets,
+                                          float scale, sbda_tensor q, sbda_tensor k, sbda_tensor v,
+                                          sbda_tensor grad_out, const float* lse, sbda_tensor grad_q,
+                                          sbda_tensor grad_k, sbda_tensor grad_v, float* workspace,
+                                          int64_t workspace_floats, void* stream) {
+  int st = validate(dtype, shape, offsets, n_offsets);
+  if (st != SBDA_OK) return st;
+  const int64_t B = shape.batch, H = shape.heads, Hkv = shape.kv_heads, L = shape.length, D = shape.head_dim;
+  if (B == 0 || H == 0 || L == 0) return SBDA_OK;
+  if (!q.data || !k.data || !v.data || !grad_out.data || !lse || !grad_q.data || !grad_k.data || !grad_v.data)
+    return SBDA_ERR_INVALID;
+  auto general = [&] {
+    return sbda_b200_backward_ex(kFamilyAuto, dtype, shape, offsets, n_offsets, scale, q, k, v, grad_out, lse,
+                                 grad_q, grad_k, grad_v, stream);
+  };
+  if (H == Hkv) return general();  // MHA: the windowed backward writes dK/dV itself
+  if (!workspace || workspace_floats < sbda_b200_backward_grouped_workspace_floats(shape) ||
+      reinterpret_cast<uintptr_t>(workspace) % 16)
+    return SBDA_ERR_INVALID;
+  const int e = elem_size(dtype);
+  V2Plan p2;
+  const bool vec = tensors_vector_ok({&q, &k, &v, &grad_out, &grad_q}, B, L, D, e, {H, Hkv, Hkv, H, H});
+  // The walk is planned per query head as for MHA; K/V rows come from kv head h / G.
+  if (!vec || D % 8 || !plan_v2(offsets, n_offsets, L, D, e, 1, B, H, &p2) || !v2_grouped_plan_ok(p2))
+    return general();
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  BwdV2Params p;
+  memset(&p, 0, sizeof(p));
+  p.G = (int)(H / Hkv);
+  p.B = (int)B;
+  p.H = (int)H;
+  p.L = (int)L;
+  p.D = (int)D;
+  p.scale = scale;
+  p.g = p2.g;
+  p.q = arg_of(q);
+  p.k = arg_of(k);
+  p.v = arg_of(v);
+  p.dout = arg_of(grad_out);
+  p.dq = arg_of(grad_q);
+  // fp32 per-query-head partials: [2][B, H, L, D], contiguous.
+  const int64_t part = B * H * L * D;
+  p.dk = TensorArg{workspace, H * L * D, L * D, D, 1};
+  p.dv = TensorArg{workspace + part, H * L * D, L * D, D, 1};
+  p.lse = lse;
+  p.status = status_ptr();
+  p.sh = single_shard(L, lse);
+  p.lse_box = p2.lse_box;
+  p.lse_tx = p2.lse_box * 4;
+  BwdMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  unsigned dummy;
+  const int hz = p2.g.halo;
+  const int lead = p2.g.mode == 2 ? p2.g.d : hz;
+  if (!(encode_map(&maps.qT, &p.slots_q, q, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.dT, &p.slots_d, grad_out, dtype, B, H, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.kT, &p.slots_k, k, dtype, B, Hkv, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.vT, &p.slots_v, v, dtype, B, Hkv, L, D, p2.pitch, p2.tile) &&
+        encode_map(&maps.qH, &dummy, q, dtype, B, H, L, D, p2.pitch, hz) &&
+        encode_map(&maps.dH, &dummy, grad_out, dtype, B, H, L, D, p2.pitch, hz) &&
+        encode_map(&maps.kH, &dummy, k, dtype, B, Hkv, L, D, p2.pitch, lead) &&
+        encode_map(&maps.vH, &dummy, v, dtype, B, Hkv, L, D, p2.pitch, lead)))
+    return general();
+  p.lse_tma = encode_lse_map(&maps.lseT, lse, B * H, L, p2.lse_box);
+  st = v2_backward_grouped(dtype, maps, p, p2, workspace, (int)Hkv, arg_of(grad_k), arg_of(grad_v), s);
+  return st == SBDA_ERR_UNSUPPORTED ? general() : st;
 }

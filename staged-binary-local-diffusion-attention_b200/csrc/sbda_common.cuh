@@ -616,6 +616,7 @@ struct FwdV2Params {
 
 struct BwdV2Params {
   int B, H, L, D;        // L: positions of this call's rows (the shard when sharded)
+  int G;                 // query heads per kv head (1 = MHA); K/V rows come from kv head h / G
   float scale;
   V2Geometry g;
   TensorArg q, k, v, dout, dq, dk, dv;
@@ -696,6 +697,12 @@ int v2_backward(int dtype, bool tma, const BwdMaps& maps, const BwdV2Params& p, 
 bool v2_normed_plan_ok(const V2Plan& pl);
 int v2_forward_normed(int dtype, const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, cudaStream_t st);
 int64_t v2_normed_workspace_floats(unsigned blocks);
+
+// Grouped-query attention on the windowed backward (sbda_v2_grouped.cu): fp32
+// per-query-head dK/dV partials in `workspace`, then a fixed-order group sum.
+bool v2_grouped_plan_ok(const V2Plan& pl);
+int v2_backward_grouped(int dtype, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, const float* workspace,
+                        int Hkv, const TensorArg& dk, const TensorArg& dv, cudaStream_t st);
 int v2_backward_normed(int dtype, const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, float* grad_q_w,
                        float* grad_k_w, float* workspace, cudaStream_t st);
 

@@ -559,7 +559,10 @@ struct BwdShape {
 // 1 (raw q still in registers), dK in phase 2 (raw k re-read from global,
 // usually an L2 hit); the norm-weight gradients are summed per CTA into
 // p.dw_partial.
-template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = BwdMaps, bool NR = false>
+// TO: element type of the dK/dV rows written.  TE (the input type) writes the
+// final gradients; float writes one query head's fp32 partials of grouped-query
+// attention (K/V rows from kv head h / G), summed per kv head afterwards.
+template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = BwdMaps, bool NR = false, typename TO = TE>
 __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const __grid_constant__ Maps maps,
                                                                   const BwdV2Params p) {
   static_assert(!NR || (TMA && LPR == 8), "norm+RoPE is fused for the copy-engine path, 8 lanes per row");
@@ -631,6 +634,7 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
     stride = 1;
   }
 
+  const int hk = h / p.G;                        // kv head of query head h (1 = MHA: hk = h)
   uint8_t* KVbase = smem;                        // nkv slots of [K rows][V rows]
   uint8_t* QDbase = KVbase + nkv * 2 * KVR * P;  // 2 slots of [Q rows][dO rows]
   // Softmax records, a ring of 2T consumers: (p0, ds0, p1, ds1) (p2, ds2, pf, dsf)
@@ -674,15 +678,15 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
       if (lc) {  // rows [j0 - d, j0 + T): a d-row box, then the tile
         const int jg = p.sh.pos0 + j0;
         int c;
-        tma_rows(kslot(0), pick_map(maps.kH, p.sh, jg - d, c), bar, p.slots_k, c, h, b);
-        tma_rows(vslot(0), pick_map(maps.vH, p.sh, jg - d, c), bar, p.slots_v, c, h, b);
-        tma_rows(kslot(0) + d * P, pick_map(maps.kT, p.sh, jg, c), bar, p.slots_k, c, h, b);
-        tma_rows(vslot(0) + d * P, pick_map(maps.vT, p.sh, jg, c), bar, p.slots_v, c, h, b);
+        tma_rows(kslot(0), pick_map(maps.kH, p.sh, jg - d, c), bar, p.slots_k, c, hk, b);
+        tma_rows(vslot(0), pick_map(maps.vH, p.sh, jg - d, c), bar, p.slots_v, c, hk, b);
+        tma_rows(kslot(0) + d * P, pick_map(maps.kT, p.sh, jg, c), bar, p.slots_k, c, hk, b);
+        tma_rows(vslot(0) + d * P, pick_map(maps.vT, p.sh, jg, c), bar, p.slots_v, c, hk, b);
       } else {
         for (int part = first; part < (chain ? 2 : 1); ++part) {
           const int slot = chain ? ((i + part) & 1) : 0;
           const int p0 = part == 0 ? j0 - Hc : j0 - d - Hc;
-          tma_kv_slot<TE, T, P>(maps, p, bar, kslot(slot), vslot(slot), p0, Hc, h, b);
+          tma_kv_slot<TE, T, P>(maps, p, bar, kslot(slot), vslot(slot), p0, Hc, hk, b);
         }
       }
     } else {
@@ -690,8 +694,8 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
       for (int part = first; part < (chain ? 2 : 1); ++part) {
         const int slot = chain ? ((i + part) & 1) : 0;
         const int p0 = part == 0 ? j0 - lead : j0 - d - Hc;
-        generic_rows<TE>(kslot(slot), p.k, b, h, p0, KVR, p.L, p.D, PE);
-        generic_rows<TE>(vslot(slot), p.v, b, h, p0, KVR, p.L, p.D, PE);
+        generic_rows<TE>(kslot(slot), p.k, b, hk, p0, KVR, p.L, p.D, PE);
+        generic_rows<TE>(vslot(slot), p.v, b, hk, p0, KVR, p.L, p.D, PE);
       }
     }
   };
@@ -719,8 +723,8 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
     return qg < p.sh.total_len ? lse_at(p.sh, bh, qg) * kLog2e : 0.f;
   };
   TE* dq = reinterpret_cast<TE*>(const_cast<void*>(p.dq.ptr)) + (long long)b * p.dq.sb + (long long)h * p.dq.sh;
-  TE* dk = reinterpret_cast<TE*>(const_cast<void*>(p.dk.ptr)) + (long long)b * p.dk.sb + (long long)h * p.dk.sh;
-  TE* dv = reinterpret_cast<TE*>(const_cast<void*>(p.dv.ptr)) + (long long)b * p.dv.sb + (long long)h * p.dv.sh;
+  TO* dk = reinterpret_cast<TO*>(const_cast<void*>(p.dk.ptr)) + (long long)b * p.dk.sb + (long long)h * p.dk.sh;
+  TO* dv = reinterpret_cast<TO*>(const_cast<void*>(p.dv.ptr)) + (long long)b * p.dv.sb + (long long)h * p.dv.sh;
 
   // Far-edge dK/dV contributions carried to the next tile of a chain walk.
   Frag carry_k[4], carry_v[4];
@@ -1018,15 +1022,15 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
           if constexpr (NR) {
             // dK of the raw row: RoPE transpose and RMSNorm Jacobian on the raw k,
             // re-read from global memory (the slot holding it is being refilled).
-            const TE* kb = reinterpret_cast<const TE*>(p.k.ptr) + (long long)b * p.k.sb + (long long)h * p.k.sh;
+            const TE* kb = reinterpret_cast<const TE*>(p.k.ptr) + (long long)b * p.k.sb + (long long)hk * p.k.sh;
             const RowWords<TE> kw = load_row_words<TE>(kb + (long long)min(j, p.L - 1) * p.k.sl, p.D, l, j < p.L);
             const Frag kx = FragIO<TE>::from_words(kw.w);
             const float rk = nr_rsqrt(fmaf(nr_row_dot(kx, kx), 1.f / 64.f, p.nk.eps));
             ak = norm_rope_grad<TE>(ak, kx, rk, l, nr_weights(p.nk.w, l), p.nk, j, p.L, dwk, j < p.L);
           }
           if (j < p.L) {
-            store_frag<TE, TMA>(dk + (long long)j * p.dk.sl, p.dk.sd, p.D, l, ak);
-            store_frag<TE, TMA>(dv + (long long)j * p.dv.sl, p.dv.sd, p.D, l, av);
+            store_frag<TO, TMA>(dk + (long long)j * p.dk.sl, p.dk.sd, p.D, l, ak);
+            store_frag<TO, TMA>(dv + (long long)j * p.dv.sl, p.dv.sd, p.D, l, av);
           }
         }
         if (chain && far) {

@@ -190,7 +190,17 @@ def sbda_backward(q: Tensor, k: Tensor, v: Tensor, grad_out: Tensor, lse: Tensor
     lib = _lib.load()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        if source_mask is None:
+        if source_mask is None and family == 0 and k.shape[1] != q.shape[1]:
+            # Grouped-query attention: windowed kernels with per-query-head fp32 dK/dV partials
+            # in a workspace, summed per kv head in a fixed order.
+            workspace = torch.empty(max(4, lib.sbda_b200_backward_grouped_workspace_floats(_shape(q, k))),
+                                    device=q.device, dtype=torch.float32)
+            status = lib.sbda_b200_backward_grouped(
+                _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
+                _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(grad_out), lse.data_ptr(),
+                _tensor_arg(dq), _tensor_arg(dk), _tensor_arg(dv), workspace.data_ptr(), workspace.numel(), stream,
+            )
+        elif source_mask is None:
             status = lib.sbda_b200_backward_ex(
                 family, _DTYPES[q.dtype], _shape(q, k), _lib.offsets_array(offsets), len(offsets), float(scale),
                 _tensor_arg(q), _tensor_arg(k), _tensor_arg(v), _tensor_arg(grad_out), lse.data_ptr(),

@@ -173,6 +173,30 @@ def test_gqa_groups(kv_heads):
         _check(1, 8, 257, 32, torch.float32, sbda_b200.topology_offsets(layer, topology="sbda"), kv_heads=kv_heads)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_gqa_windowed_every_walk_mode(dtype):
+    """Grouped-query attention on the windowed kernels (forward from kv head h / G; backward with
+    fp32 per-query-head dK/dV partials and a fixed-order group sum), on every walk mode of the
+    backward and groups of 2, 4 and 8, against the fp64 oracle."""
+    for layer in (1, 2, 3, 6, 7, 9, 12):
+        offsets = sbda_b200.topology_offsets(layer, topology="sbda")
+        for heads, kv_heads in ((4, 2), (8, 2), (8, 1)):
+            _check(1, heads, 3000, 64, dtype, offsets, kv_heads=kv_heads, seed=layer * 7 + heads)
+
+
+def test_gqa_windowed_deterministic_and_matches_general_family():
+    q, k, v, do = _inputs(2, 8, 5000, 64, torch.bfloat16, kv_heads=2, seed=21)
+    offsets = sbda_b200.topology_offsets(10, topology="sbda")
+    first = _run(q, k, v, do, offsets, gqa=True)
+    second = _run(q, k, v, do, offsets, gqa=True)
+    for a, b in zip(first, second):
+        assert torch.equal(a, b)
+    with sbda_b200.kernel_family("general"):
+        general = _run(q, k, v, do, offsets, gqa=True)
+    for a, b in zip(first, general):
+        torch.testing.assert_close(a.float(), b.float(), rtol=2.0 ** -7, atol=2e-2)
+
+
 def test_other_offset_sets(kernel_path):
     for offsets in ((0,), (0, 3), (0, 1, 2), (0, 1, 2, 3), (0, 5, 64), (0, 2, 100), (0, 1, 64, 200),
                     (4, 0), (0, 1, 2, 65), (2, 0, 1, 128), (0, 1, 2, 32), (0, 1, 2, 63), (0, 1, 2, 399),
