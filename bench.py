@@ -340,6 +340,19 @@ def run_b200(args) -> None:
     clocks = sampler.stop()
     step_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
 
+    # Per-kernel durations (separate pass with an event pair around every launch).
+    for _ in range(2):
+        step(record=True)
+    torch.cuda.synchronize()
+    fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in fwd_events)
+    bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in bwd_events)
+    # per-layer launch times (forward in layer order; backward recorded in reverse)
+    n_rec = len(fwd_events) // layers
+    fwd_layer_ms = [statistics.mean(fwd_events[k * layers + j][0].elapsed_time(fwd_events[k * layers + j][1])
+                                    for k in range(n_rec)) for j in range(layers)]
+    bwd_layer_ms = [statistics.mean(bwd_events[k * layers + (layers - 1 - j)][0].elapsed_time(
+        bwd_events[k * layers + (layers - 1 - j)][1]) for k in range(n_rec)) for j in range(layers)]
+
     # Host time to issue one step's 40 launches (no synchronisation inside), median of 3.
     host_ms = []
     for _ in range(3):
@@ -379,19 +392,6 @@ def run_b200(args) -> None:
         del graph
     except RuntimeError as err:  # reported, not fatal for the bench line
         graph_info = {"error": str(err).splitlines()[0][:200]}
-
-    # Per-kernel durations (separate pass with an event pair around every launch).
-    for _ in range(2):
-        step(record=True)
-    torch.cuda.synchronize()
-    fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in fwd_events)
-    bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in bwd_events)
-    # per-layer launch times (forward in layer order; backward recorded in reverse)
-    n_rec = len(fwd_events) // layers
-    fwd_layer_ms = [statistics.mean(fwd_events[k * layers + j][0].elapsed_time(fwd_events[k * layers + j][1])
-                                    for k in range(n_rec)) for j in range(layers)]
-    bwd_layer_ms = [statistics.mean(bwd_events[k * layers + (layers - 1 - j)][0].elapsed_time(
-        bwd_events[k * layers + (layers - 1 - j)][1]) for k in range(n_rec)) for j in range(layers)]
 
     rows = H * L
     e = 2
