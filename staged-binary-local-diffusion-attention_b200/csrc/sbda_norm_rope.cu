@@ -244,13 +244,14 @@ __global__ void __launch_bounds__(1024) sbda_norm_weight_reduce_kernel(const flo
 // head_dim 64 with layouts the vector path takes (16-byte aligned rows and
 // strides, unit channel stride, 16-byte aligned tables and weight): 8 lanes
 // per row, each lane holding 8 channels in registers, the rotation partner
-// one shuffle away (lane ^ 4).  A CTA iteration covers 64 rows: row group g
-// takes rows base + 16 i + g (i = 0..3), so each warp reads 4 consecutive
-// rows (512 contiguous bytes in the [B, L, H, D] layout) per load, and a lane
-// has 4 loads in flight before it computes.
+// one shuffle away (lane ^ 4).  A CTA iteration covers 16 * R rows (R rows
+// per lane: kNRFwdRows, kNRBwdRows): row group g takes rows base + 16 i + g
+// (i < R), so each warp reads 4 consecutive rows (512 contiguous bytes in the
+// [B, L, H, D] layout) per load, and a lane has R rows' loads in flight before
+// it computes.
 // --------------------------------------------------------------------------
 
-constexpr int kNR64Rows = 64;  // rows per CTA iteration
+constexpr int kNRFwdRows = 4;  // forward: rows per lane per CTA iteration (16 row groups per CTA)
 
 // n / d for 0 <= n < 2^31 by a multiply and a shift: division by an invariant
 // integer with a rounded-up multiplier (Granlund and Montgomery, "Division by
@@ -294,13 +295,13 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_kernel(const NormRop
   const Frag w = nr_weights(p.w, l);
   const TE* x = reinterpret_cast<const TE*>(p.x.ptr);
   TE* y = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
-  for (long long base = (long long)blockIdx.x * kNR64Rows; base < rows_total;
-       base += (long long)gridDim.x * kNR64Rows) {
-    RowWords<TE> in[4];
-    int pos[4];
-    long long yo[4];
+  for (long long base = (long long)blockIdx.x * 16 * kNRFwdRows; base < rows_total;
+       base += (long long)gridDim.x * 16 * kNRFwdRows) {
+    RowWords<TE> in[kNRFwdRows];
+    int pos[kNRFwdRows];
+    long long yo[kNRFwdRows];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kNRFwdRows; ++i) {
       const long long row = base + 16 * i + grp;
       const bool live = row < rows_total;
       int b, h;
@@ -309,19 +310,22 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_kernel(const NormRop
       in[i] = load_row_words<TE>(x + nr_offset(p.x, b, pos[i], h), 64, l, live);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kNRFwdRows; ++i) {
       const Frag z = norm_rope_frag<TE>(FragIO<TE>::from_words(in[i].w), l, w, a, pos[i], p.L, nullptr);
       if (base + 16 * i + grp < rows_total) store_frag<TE, true>(y + yo[i], 1, 64, l, z);
     }
   }
 }
 
-// One CTA iteration's input rows of the backward: x and dy of 4 rows per lane.
+// Rows per lane per iteration of the backward (16 * kNRBwdRows rows per CTA iteration).
+constexpr int kNRBwdRows = 2;
+
+// One CTA iteration's input rows of the backward: x and dy of kNRBwdRows rows per lane.
 template <typename TE>
 struct NR64BwdRows {
-  RowWords<TE> x[4], g[4];
-  int pos[4];
-  long long dxo[4];
+  RowWords<TE> x[kNRBwdRows], g[kNRBwdRows];
+  int pos[kNRBwdRows];
+  long long dxo[kNRBwdRows];
 };
 
 template <typename TE>
@@ -331,7 +335,7 @@ __device__ __forceinline__ void nr64_bwd_load(NR64BwdRows<TE>& r, const NormRope
   const TE* x = reinterpret_cast<const TE*>(p.x.ptr);
   const TE* dy = reinterpret_cast<const TE*>(p.dy.ptr);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < kNRBwdRows; ++i) {
     const long long row = base + 16 * i + grp;
     const bool live = row < rows_total;
     int b, h;
@@ -342,7 +346,7 @@ __device__ __forceinline__ void nr64_bwd_load(NR64BwdRows<TE>& r, const NormRope
   }
 }
 
-// Loads of an iteration are issued together (8 per lane), then its math runs.
+// Loads of an iteration are issued together (2 per row per lane), then its math runs.
 // (Loading the next iteration's rows during this one's math needs ~160
 // registers: 3 CTAs per SM instead of 4, and measured 22 % slower.)
 template <typename TE>
@@ -351,16 +355,16 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_kernel(const NormRop
   __shared__ float sums[16 * 64];
   const int l = threadIdx.x & 7, grp = threadIdx.x >> 3;
   const long long rows_total = (long long)p.B * p.L * p.H;
-  const long long stride = (long long)gridDim.x * kNR64Rows;
+  const long long stride = (long long)gridDim.x * 16 * kNRBwdRows;
   const NormRopeArgs a{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps};
   const Frag w = nr_weights(p.w, l);
   TE* dx = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
   Frag dw = frag_zero();
-  for (long long base = (long long)blockIdx.x * kNR64Rows; base < rows_total; base += stride) {
+  for (long long base = (long long)blockIdx.x * 16 * kNRBwdRows; base < rows_total; base += stride) {
     NR64BwdRows<TE> cur;
     nr64_bwd_load(cur, p, base, rows_total, grp, l, fh, fl);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kNRBwdRows; ++i) {
       const bool live = base + 16 * i + grp < rows_total;
       const Frag xv = FragIO<TE>::from_words(cur.x[i].w);
       const float r = nr_rsqrt(fmaf(nr_row_dot(xv, xv), 1.f / 64.f, p.eps));
@@ -403,7 +407,7 @@ template <typename TE>
 int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
   if (nr_use64(p, sizeof(TE), false)) {
     const long long rows = (long long)p.B * p.L * p.H;
-    const long long grid = (rows + kNR64Rows - 1) / kNR64Rows;
+    const long long grid = (rows + 16 * kNRFwdRows - 1) / (16 * kNRFwdRows);
     sbda_norm_rope64_fwd_kernel<TE><<<(unsigned)(grid < (1ll << 20) ? grid : (1ll << 20)), 128, 0, st>>>(
         p, make_fastdiv((unsigned)p.H), make_fastdiv((unsigned)p.L));
     return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
