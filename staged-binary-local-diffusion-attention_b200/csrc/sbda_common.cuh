@@ -126,6 +126,37 @@ __device__ __forceinline__ float lse_at(const ShardInfo& s, long long bh, int q)
 }
 
 // --------------------------------------------------------------------------
+// Programmatic dependent launch.  The windowed kernels are launched with
+// programmatic stream serialization (launch_chained): their CTAs may be
+// scheduled while the previous kernel on the stream drains its last wave, and
+// they call grid_dependency_sync() before their first global memory access,
+// which waits until that kernel has completed and its writes are visible.  The
+// same call lets the next chained kernel be scheduled once every CTA of this
+// grid has started.  Without the launch attribute both instructions are no-ops.
+// --------------------------------------------------------------------------
+
+__device__ __forceinline__ void grid_dependency_sync() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_chained(void (*kern)(Params...), unsigned grid, size_t smem, cudaStream_t st,
+                                  const Args&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr = {};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// --------------------------------------------------------------------------
 // Device helpers: mbarrier + TMA (inline PTX), element packing
 // --------------------------------------------------------------------------
 
@@ -535,26 +566,28 @@ __device__ __forceinline__ float lane_group_sum(float x) {
   return x;
 }
 
-// Reduce-scatter over the 8 lanes of a row group (lane index l = lane % 8):
-// eight per-lane partial sums in, the group total of x[l] out on lane l.
-// Three halving exchanges (4 + 2 + 1 shuffles) instead of eight all-reduces.
-__device__ __forceinline__ float group8_reduce_scatter8(const float (&x)[8], int l) {
+// Reduce-scatter over the 8 lanes of a row group of four (x[s], x[s + 4]) pairs
+// (lane index l = lane % 8): the group totals of x[l & 3] and x[(l & 3) + 4]
+// out on lanes l and l ^ 4: two halving exchanges (4 + 2 shuffles), then an
+// exchange of both values between lanes l and l ^ 4 (2 shuffles).  Both lanes of
+// a source then hold its q.k and dO.v, so its softmax terms need no further
+// exchange before the sum over sources.
+__device__ __forceinline__ float2 group8_reduce_scatter_pairs(const float (&x)[8], int l) {
   const unsigned full = 0xffffffffu;
-  const bool h4 = l & 4, h2 = l & 2, h1 = l & 1;
+  const bool h1 = l & 1, h2 = l & 2;
   float w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float send = h4 ? x[i] : x[i + 4];
-    w[i] = (h4 ? x[i + 4] : x[i]) + __shfl_xor_sync(full, send, 4);
+  for (int j = 0; j < 4; ++j) {
+    const float send = h1 ? x[2 * j] : x[2 * j + 1];
+    w[j] = (h1 ? x[2 * j + 1] : x[2 * j]) + __shfl_xor_sync(full, send, 1);
   }
   float z[2];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float send = h2 ? w[i] : w[i + 2];
-    z[i] = (h2 ? w[i + 2] : w[i]) + __shfl_xor_sync(full, send, 2);
+  for (int j = 0; j < 2; ++j) {
+    const float send = h2 ? w[2 * j] : w[2 * j + 1];
+    z[j] = (h2 ? w[2 * j + 1] : w[2 * j]) + __shfl_xor_sync(full, send, 2);
   }
-  const float send = h1 ? z[0] : z[1];
-  return (h1 ? z[1] : z[0]) + __shfl_xor_sync(full, send, 1);
+  return make_float2(z[0] + __shfl_xor_sync(full, z[0], 4), z[1] + __shfl_xor_sync(full, z[1], 4));
 }
 
 // Four per-lane partial sums over the 8 lanes of a row group: the group total

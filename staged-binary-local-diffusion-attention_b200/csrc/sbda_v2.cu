@@ -17,8 +17,7 @@ int launch_fwd_v2(const Maps& maps, const FwdV2Params& p, const V2Plan& pl, cuda
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SBDA_ERR_CUDA;
   const long long blocks = (long long)p.B * p.H * pl.g.nT;
-  kern<<<(unsigned)blocks, kThreads, smem, st>>>(maps, p);
-  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  return launch_chained(kern, (unsigned)blocks, smem, st, maps, p) == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
 template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps>
@@ -26,8 +25,7 @@ int launch_bwd_v2(const Maps& maps, const BwdV2Params& p, const V2Plan& pl, cuda
   auto kern = sbda_bwd_v2_kernel<TE, LPR, TMA, SHAPE, Maps>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
-  kern<<<pl.blocks_bwd, kThreads, pl.smem_bwd, st>>>(maps, p);
-  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  return launch_chained(kern, pl.blocks_bwd, pl.smem_bwd, st, maps, p) == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
 template <typename TE, bool TMA, typename Maps>

@@ -23,8 +23,7 @@ int launch_bwd_grouped(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& 
   auto kern = sbda_bwd_v2_kernel<TE, 8, true, SHAPE, BwdMaps, false, float>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
-  kern<<<pl.blocks_bwd, kThreads, pl.smem_bwd, st>>>(maps, p);
-  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  return launch_chained(kern, pl.blocks_bwd, pl.smem_bwd, st, maps, p) == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
 template <typename TE>

@@ -298,6 +298,7 @@ __device__ __forceinline__ void nr_write_partials(float* partial, float* scratch
 template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = FwdMaps, bool NR = false>
 __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_constant__ Maps maps,
                                                                const FwdV2Params p) {
+  grid_dependency_sync();  // before any global memory access
   static_assert(!NR || (TMA && LPR == 8), "norm+RoPE is fused for the copy-engine path, 8 lanes per row");
   constexpr int T = v2_tile(LPR);
   constexpr int P = LPR * FragIO<TE>::kLaneBytes;
@@ -565,6 +566,7 @@ struct BwdShape {
 template <typename TE, int LPR, bool TMA, int SHAPE, typename Maps = BwdMaps, bool NR = false, typename TO = TE>
 __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const __grid_constant__ Maps maps,
                                                                   const BwdV2Params p) {
+  grid_dependency_sync();  // before any global memory access
   static_assert(!NR || (TMA && LPR == 8), "norm+RoPE is fused for the copy-engine path, 8 lanes per row");
   constexpr int T = v2_tile(LPR);
   constexpr int P = LPR * FragIO<TE>::kLaneBytes;
@@ -804,8 +806,9 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
       }
       const Frag df = FragIO<TE>::load(Ds + c * P, l);
       if constexpr (LPR == 8) {
-        // Reduce-scatter softmax: after the exchange lane l holds q.k of source l
-        // (l < 4) or dO.v of source l - 4; each source's p and ds are formed once.
+        // Reduce-scatter softmax: after the exchange lanes l and l ^ 4 both hold q.k
+        // and dO.v of source l & 3 and form its p and ds (the same values on both),
+        // so p needs no exchange between the score lanes and the dO.v lanes.
         float x[8];
         x[0] = frag_dot(qf, k0);
         x[4] = frag_dot(df, v0);
@@ -822,17 +825,16 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
           x[7] = frag_dot(df, vf);
         }
         const unsigned full = 0xffffffffu;
-        const float val = group8_reduce_scatter8(x, l);
+        const float2 ab = group8_reduce_scatter_pairs(x, l);  // (q.k, dO.v) of source l & 3
         const bool inr = qg < p.sh.total_len;
-        const bool live = l < 4 && src_has && inr && qg >= src_off;
-        const float pa = live ? fast_exp2(fmaf(val, c1, -lq2)) : 0.f;
-        const float ps = __shfl_xor_sync(full, pa, 4);  // lanes 4..7: p of source l - 4
-        const float t = l >= 4 ? ps * val : 0.f;
+        const bool live = src_has && inr && qg >= src_off;
+        const float ps = live ? fast_exp2(fmaf(ab.x, c1, -lq2)) : 0.f;
+        const float t = ps * ab.y;
         float delta = t + __shfl_xor_sync(full, t, 1);
         delta += __shfl_xor_sync(full, delta, 2);
-        const float ds = ps * (val - delta) * scale;  // lanes 4..7
-        const float d0 = __shfl_sync(full, ds, 4, 8), d1 = __shfl_sync(full, ds, 5, 8);
-        const float d2 = __shfl_sync(full, ds, 6, 8), dfw = __shfl_sync(full, ds, 7, 8);
+        const float ds = ps * (ab.y - delta) * scale;
+        const float d0 = __shfl_sync(full, ds, 0, 8), d1 = __shfl_sync(full, ds, 1, 8);
+        const float d2 = __shfl_sync(full, ds, 2, 8), dfw = __shfl_sync(full, ds, 3, 8);
         const bool store_q = act && c < T && inr && !is_pre;
         if constexpr (NR) {
           // dQ of the raw row: RoPE transpose and RMSNorm Jacobian (every lane shuffles).
@@ -851,7 +853,7 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
           if (far) frag_axpy(gq, dfw, kf);
           store_frag<TE, TMA>(dq + (long long)q * p.dq.sl, p.dq.sd, p.D, l, gq);
         }
-        if (act && l >= 4) reinterpret_cast<float2*>(erow)[l - 4] = make_float2(ps, ds);
+        if (act && l < 4) reinterpret_cast<float2*>(erow)[l] = make_float2(ps, ds);
         return;
       }
       const float a0 = lane_group_sum<LPR>(frag_dot(qf, k0));

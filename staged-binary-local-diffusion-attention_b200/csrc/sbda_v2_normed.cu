@@ -18,8 +18,7 @@ int launch_fwd_nr(const FwdMaps& maps, const FwdV2Params& p, const V2Plan& pl, c
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SBDA_ERR_CUDA;
   const long long blocks = (long long)p.B * p.H * pl.g.nT;
-  kern<<<(unsigned)blocks, kThreads, smem, st>>>(maps, p);
-  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  return launch_chained(kern, (unsigned)blocks, smem, st, maps, p) == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
 template <typename TE, int SHAPE>
@@ -27,8 +26,7 @@ int launch_bwd_nr(const BwdMaps& maps, const BwdV2Params& p, const V2Plan& pl, c
   auto kern = sbda_bwd_v2_kernel<TE, 8, true, SHAPE, BwdMaps, true>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem_bwd) != cudaSuccess)
     return SBDA_ERR_CUDA;
-  kern<<<pl.blocks_bwd, kThreads, pl.smem_bwd, st>>>(maps, p);
-  return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  return launch_chained(kern, pl.blocks_bwd, pl.smem_bwd, st, maps, p) == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
 }
 
 template <typename TE>
