@@ -120,6 +120,21 @@ __device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap (&m)[kM
 }
 
 // Log-sum-exp of (b, h) at global position q (0 <= q < total_len).
+// This rank's own map (one GPU: the map itself), and whether the call's local
+// rows [lo, hi) all lie in this rank's shard, so that every box over them can use
+// that map at local coordinates without an owner search.  One GPU: always (rows
+// outside the sequence read as the map's zero fill).  The copies of a step are
+// issued by one thread on the step's critical path; the owner search for each of
+// a step's boxes was most of the sharded kernels' extra time.
+__device__ __forceinline__ const CUtensorMap* own_map(const CUtensorMap& m, const ShardInfo&) { return &m; }
+__device__ __forceinline__ const CUtensorMap* own_map(const CUtensorMap (&m)[kMaxShards], const ShardInfo& s) {
+  return &m[s.rank];
+}
+__device__ __forceinline__ bool own_rows(const CUtensorMap&, const ShardInfo&, int, int) { return true; }
+__device__ __forceinline__ bool own_rows(const CUtensorMap (&)[kMaxShards], const ShardInfo& s, int lo, int hi) {
+  return lo >= 0 && hi <= s.shard_len;
+}
+
 __device__ __forceinline__ float lse_at(const ShardInfo& s, long long bh, int q) {
   const int owner = s.world == 1 ? 0 : q / s.shard_len;
   return s.lse[owner][bh * s.shard_len + (q - owner * s.shard_len)];

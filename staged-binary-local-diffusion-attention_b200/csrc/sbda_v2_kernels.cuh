@@ -343,17 +343,30 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
     }
     __syncthreads();
     if (tid == 0) {
-      // Each box lies in one rank's shard; pick_map gives its map and local row.
+      // Each box lies in one rank's shard: this rank's map at local rows, or
+      // (shards) pick_map gives the owner's map and row.
       const int ig = p.sh.pos0 + i0;
       int c;
       mbar_arrive_expect_tx(bar, (uint32_t)((2 * (T + lead) + (far && !near_far ? 2 * T : 0)) * P));
-      tma_rows(Kn, pick_map(maps.kH, p.sh, ig - lead, c), bar, p.slots_k, c, hk, b);
-      tma_rows(Vn, pick_map(maps.vH, p.sh, ig - lead, c), bar, p.slots_v, c, hk, b);
-      tma_rows(Kn + lead * P, pick_map(maps.kT, p.sh, ig, c), bar, p.slots_k, c, hk, b);
-      tma_rows(Vn + lead * P, pick_map(maps.vT, p.sh, ig, c), bar, p.slots_v, c, hk, b);
+      if (own_rows(maps.kT, p.sh, i0 - lead, i0 + T)) {
+        tma_rows(Kn, own_map(maps.kH, p.sh), bar, p.slots_k, i0 - lead, hk, b);
+        tma_rows(Vn, own_map(maps.vH, p.sh), bar, p.slots_v, i0 - lead, hk, b);
+        tma_rows(Kn + lead * P, own_map(maps.kT, p.sh), bar, p.slots_k, i0, hk, b);
+        tma_rows(Vn + lead * P, own_map(maps.vT, p.sh), bar, p.slots_v, i0, hk, b);
+      } else {
+        tma_rows(Kn, pick_map(maps.kH, p.sh, ig - lead, c), bar, p.slots_k, c, hk, b);
+        tma_rows(Vn, pick_map(maps.vH, p.sh, ig - lead, c), bar, p.slots_v, c, hk, b);
+        tma_rows(Kn + lead * P, pick_map(maps.kT, p.sh, ig, c), bar, p.slots_k, c, hk, b);
+        tma_rows(Vn + lead * P, pick_map(maps.vT, p.sh, ig, c), bar, p.slots_v, c, hk, b);
+      }
       if (far && !near_far) {
-        tma_rows(Kf, pick_map(maps.kT, p.sh, ig - g.d, c), bar, p.slots_k, c, hk, b);
-        tma_rows(Vf, pick_map(maps.vT, p.sh, ig - g.d, c), bar, p.slots_v, c, hk, b);
+        if (own_rows(maps.kT, p.sh, i0 - g.d, i0 - g.d + T)) {
+          tma_rows(Kf, own_map(maps.kT, p.sh), bar, p.slots_k, i0 - g.d, hk, b);
+          tma_rows(Vf, own_map(maps.vT, p.sh), bar, p.slots_v, i0 - g.d, hk, b);
+        } else {
+          tma_rows(Kf, pick_map(maps.kT, p.sh, ig - g.d, c), bar, p.slots_k, c, hk, b);
+          tma_rows(Vf, pick_map(maps.vT, p.sh, ig - g.d, c), bar, p.slots_v, c, hk, b);
+        }
       }
     }
     // Q rows of this group, in flight while the K/V copies land.
@@ -496,6 +509,15 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
 template <typename TE, int T, int P, typename Maps>
 __device__ __forceinline__ void tma_kv_slot(const Maps& maps, const BwdV2Params& p, uint64_t* bar,
                                             uint8_t* K, uint8_t* V, int p0, int halo, int h, int b) {
+  if (own_rows(maps.kT, p.sh, p0, p0 + 2 * halo + T)) {
+    tma_rows(K, own_map(maps.kH, p.sh), bar, p.slots_k, p0, h, b);
+    tma_rows(V, own_map(maps.vH, p.sh), bar, p.slots_v, p0, h, b);
+    tma_rows(K + halo * P, own_map(maps.kT, p.sh), bar, p.slots_k, p0 + halo, h, b);
+    tma_rows(V + halo * P, own_map(maps.vT, p.sh), bar, p.slots_v, p0 + halo, h, b);
+    tma_rows(K + (halo + T) * P, own_map(maps.kH, p.sh), bar, p.slots_k, p0 + halo + T, h, b);
+    tma_rows(V + (halo + T) * P, own_map(maps.vH, p.sh), bar, p.slots_v, p0 + halo + T, h, b);
+    return;
+  }
   const int g0 = p.sh.pos0 + p0;
   int c;
   tma_rows(K, pick_map(maps.kH, p.sh, g0, c), bar, p.slots_k, c, h, b);
@@ -509,6 +531,13 @@ __device__ __forceinline__ void tma_kv_slot(const Maps& maps, const BwdV2Params&
 template <typename TE, int T, int P, typename Maps>
 __device__ __forceinline__ void tma_qd_slot(const Maps& maps, const BwdV2Params& p, uint64_t* bar,
                                             uint8_t* Q, uint8_t* Dd, int j0, int halo, int h, int b) {
+  if (own_rows(maps.qT, p.sh, j0, j0 + T + halo)) {
+    tma_rows(Q, own_map(maps.qT, p.sh), bar, p.slots_q, j0, h, b);
+    tma_rows(Dd, own_map(maps.dT, p.sh), bar, p.slots_d, j0, h, b);
+    tma_rows(Q + T * P, own_map(maps.qH, p.sh), bar, p.slots_q, j0 + T, h, b);
+    tma_rows(Dd + T * P, own_map(maps.dH, p.sh), bar, p.slots_d, j0 + T, h, b);
+    return;
+  }
   const int g0 = p.sh.pos0 + j0;
   int c;
   tma_rows(Q, pick_map(maps.qT, p.sh, g0, c), bar, p.slots_q, c, h, b);
@@ -523,12 +552,18 @@ __device__ __forceinline__ void tma_qd_slot(const Maps& maps, const BwdV2Params&
 // zero-filled); both boxes start at tile-aligned rows.
 template <int T>
 __device__ __forceinline__ void tma_lse_slot(const BwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
-                                             float* dst, int j0, int row) {
+                                             float* dst, int j0, int halo, int row) {
   tma_2d(dst, &maps.lseT, bar, j0, row);
 }
 template <int T>
 __device__ __forceinline__ void tma_lse_slot(const ShardBwdMaps& maps, const BwdV2Params& p, uint64_t* bar,
-                                             float* dst, int j0, int row) {
+                                             float* dst, int j0, int halo, int row) {
+  // The halo box may run past the consumers used (rows T + halo.. are padding).
+  if (own_rows(maps.lseT, p.sh, j0, j0 + T + halo)) {
+    tma_2d(dst, own_map(maps.lseT, p.sh), bar, j0, row);
+    tma_2d(dst + T, own_map(maps.lseH, p.sh), bar, j0 + T, row);
+    return;
+  }
   const int g0 = p.sh.pos0 + j0;
   int c;
   const CUtensorMap* m = pick_map(maps.lseT, p.sh, g0, c);
@@ -662,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
       uint64_t* bar = bars + (i & 1);
       mbar_arrive_expect_tx(bar, (uint32_t)(2 * QDR * P + (p.lse_tma ? p.lse_tx : 0)));
       tma_qd_slot<TE, T, P>(maps, p, bar, qslot(i & 1), dslot(i & 1), j0, Hc, h, b);
-      if (p.lse_tma) tma_lse_slot<T>(maps, p, bar, LSEs + (i & 1) * p.lse_box, j0, b * p.H + h);
+      if (p.lse_tma) tma_lse_slot<T>(maps, p, bar, LSEs + (i & 1) * p.lse_box, j0, Hc, b * p.H + h);
     } else {
       constexpr int PE = P / sizeof(TE);
       generic_rows<TE>(qslot(i & 1), p.q, b, h, j0, QDR, p.L, p.D, PE);
@@ -677,7 +712,12 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
     if constexpr (TMA) {
       uint64_t* bar = bars + (i & 1);
       mbar_arrive_expect_tx(bar, (uint32_t)((chain && i == 0 ? 2 : 1) * 2 * KVR * P));
-      if (lc) {  // rows [j0 - d, j0 + T): a d-row box, then the tile
+      if (lc && own_rows(maps.kT, p.sh, j0 - d, j0 + T)) {  // rows [j0 - d, j0 + T): a d-row box, then the tile
+        tma_rows(kslot(0), own_map(maps.kH, p.sh), bar, p.slots_k, j0 - d, hk, b);
+        tma_rows(vslot(0), own_map(maps.vH, p.sh), bar, p.slots_v, j0 - d, hk, b);
+        tma_rows(kslot(0) + d * P, own_map(maps.kT, p.sh), bar, p.slots_k, j0, hk, b);
+        tma_rows(vslot(0) + d * P, own_map(maps.vT, p.sh), bar, p.slots_v, j0, hk, b);
+      } else if (lc) {
         const int jg = p.sh.pos0 + j0;
         int c;
         tma_rows(kslot(0), pick_map(maps.kH, p.sh, jg - d, c), bar, p.slots_k, c, hk, b);
