@@ -62,6 +62,9 @@ def parse_args():
     p.add_argument("--heads", type=int, default=4)
     p.add_argument("--head-dim", type=int, default=64)
     p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--e2e-copy-streams", type=int, default=1,
+                   help="copy streams per direction in the e2e leg (a layer's tensors alternate between them); "
+                        "1, 2 and 3 measured alike, 40-43 GB/s host-to-device: the host link is the bound")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-blocks", action="store_true",
@@ -475,10 +478,11 @@ def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
     """Public API (fused_sbda_key_backward + autograd) with pinned host buffers.
 
     Every layer of every step copies q, k, v, dO host->device and dQ, dK, dV
-    device->host inside the timed region.  The copies run on two side streams
-    (PCIe is full duplex): layer l+1's inputs land in the second of two device
-    buffer sets while layer l computes, and layer l's gradients drain while
-    layer l+1 computes; events order every buffer reuse.
+    device->host inside the timed region.  The copies run on side streams
+    (PCIe is full duplex; ``--e2e-copy-streams`` per direction, a layer's
+    tensors alternating between them): layer l+1's inputs land in the second
+    of two device buffer sets while layer l computes, and layer l's gradients
+    drain while layer l+1 computes; events order every buffer reuse.
     """
     import sbda_b200
 
@@ -490,42 +494,48 @@ def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
                 for _ in range(2)]
     off_tensors = [torch.tensor(o, dtype=torch.int32, device=device) for o in offsets]
     compute = torch.cuda.current_stream(device)
-    h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    n_copy = max(1, args.e2e_copy_streams)
+    h2d = [torch.cuda.Stream(device) for _ in range(n_copy)]
+    d2h = [torch.cuda.Stream(device) for _ in range(n_copy)]
 
     def step():
-        ready = [torch.cuda.Event(), torch.cuda.Event()]   # inputs of a buffer set landed
-        freed = [torch.cuda.Event(), torch.cuda.Event()]   # compute is done with a buffer set
-        h2d.wait_stream(compute)
-        d2h.wait_stream(compute)
+        # per buffer set: inputs landed (one event per copy stream), compute done with it
+        ready = [[torch.cuda.Event() for _ in h2d] for _ in range(2)]
+        freed = [torch.cuda.Event(), torch.cuda.Event()]
+        for st in h2d + d2h:
+            st.wait_stream(compute)
 
         def load(layer):
             s = layer % 2
-            with torch.cuda.stream(h2d):
-                if layer >= 2:
-                    h2d.wait_event(freed[s])
-                for dst, src in zip(dev_sets[s], host_in):
-                    dst.copy_(src, non_blocking=True)
-                ready[s].record(h2d)
+            for i, st in enumerate(h2d):
+                with torch.cuda.stream(st):
+                    if layer >= 2:
+                        st.wait_event(freed[s])
+                    for j in range(i, len(host_in), n_copy):
+                        dev_sets[s][j].copy_(host_in[j], non_blocking=True)
+                    ready[s][i].record(st)
 
         load(0)
         for layer in range(layers):
             s = layer % 2
             if layer + 1 < layers:
                 load(layer + 1)
-            compute.wait_event(ready[s])
+            for ev in ready[s]:
+                compute.wait_event(ev)
             q, k, v = (t.permute(0, 2, 1, 3).requires_grad_() for t in dev_sets[s][:3])
             out = sbda_b200.fused_sbda_key_backward(q, k, v, off_tensors[layer])
             out.backward(dev_sets[s][3].permute(0, 2, 1, 3))
             freed[s].record(compute)
             grads = (q.grad, k.grad, v.grad)
-            d2h.wait_stream(compute)
-            with torch.cuda.stream(d2h):
-                for dst, src in zip(host_out, grads):
-                    dst.copy_(src.permute(0, 2, 1, 3), non_blocking=True)
-            for t in grads:
-                t.record_stream(d2h)
-        compute.wait_stream(h2d)
-        compute.wait_stream(d2h)
+            for i, st in enumerate(d2h):
+                st.wait_stream(compute)
+                with torch.cuda.stream(st):
+                    for j in range(i, len(grads), n_copy):
+                        host_out[j].copy_(grads[j].permute(0, 2, 1, 3), non_blocking=True)
+                for j in range(i, len(grads), n_copy):
+                    grads[j].record_stream(st)
+        for st in h2d + d2h:
+            compute.wait_stream(st)
 
     step()
     torch.cuda.synchronize()
@@ -546,7 +556,7 @@ def measure_e2e(args, device, offsets, barrier, max_over_ranks, world) -> dict:
             "d2h_bytes_per_step": 3 * tensor_bytes * layers, "ms_per_step": ms, "steps": steps,
             "ms_per_step_min_max": [min(per_step), max(per_step)],
             "api": "sbda_b200.fused_sbda_key_backward + autograd backward, pinned host buffers; "
-                   "copies on two side streams overlapped with compute"}
+                   f"copies on {n_copy} side stream(s) per direction, overlapped with compute"}
 
 
 class L2Flush:
