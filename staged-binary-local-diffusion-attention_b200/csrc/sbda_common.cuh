@@ -119,7 +119,6 @@ __device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap (&m)[kM
   return &m[owner];
 }
 
-// Log-sum-exp of (b, h) at global position q (0 <= q < total_len).
 // This rank's own map (one GPU: the map itself), and whether the call's local
 // rows [lo, hi) all lie in this rank's shard, so that every box over them can use
 // that map at local coordinates without an owner search.  One GPU: always (rows
@@ -135,6 +134,7 @@ __device__ __forceinline__ bool own_rows(const CUtensorMap (&)[kMaxShards], cons
   return lo >= 0 && hi <= s.shard_len;
 }
 
+// Log-sum-exp of (b, h) at global position q (0 <= q < total_len).
 __device__ __forceinline__ float lse_at(const ShardInfo& s, long long bh, int q) {
   const int owner = s.world == 1 ? 0 : q / s.shard_len;
   return s.lse[owner][bh * s.shard_len + (q - owner * s.shard_len)];
@@ -706,6 +706,20 @@ __host__ __device__ constexpr int v2_tile(int lpr) { return 4 * (kThreads / lpr)
 // Floats of the backward's softmax-record ring for tile height T: 2T records of
 // 8 floats plus 4 floats of padding per 4 records.
 __host__ __device__ constexpr int v2_ring_floats(int T) { return 2 * T * 8 + (2 * T / 4) * 4; }
+
+// Host helpers shared by the translation units (sbda_api.cu): the device's
+// fault word (kernels report expired waits into it) and its SM count.
+unsigned* status_ptr();
+int sm_count();
+
+// Untiled bulk copy global -> this CTA's shared memory, completion counted on
+// `bar` (both addresses 16-byte aligned, `bytes` a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
 
 // Host-side launchers (defined in sbda_v1.cu / sbda_v2.cu).
 struct Plan {

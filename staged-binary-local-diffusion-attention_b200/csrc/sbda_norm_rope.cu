@@ -44,6 +44,7 @@ struct NormRopeParams {
   const void* sin_t;
   long long table_offset;   // table row of position 0
   float* partial;           // backward: [gridDim.x, D] fp32 weight-gradient partials
+  unsigned* status;         // fault word (bounded copy waits of the ring kernels)
 };
 
 template <typename TE>
@@ -388,6 +389,167 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_kernel(const NormRop
   }
 }
 
+// --------------------------------------------------------------------------
+// head_dim 64 on contiguous [B, L, H, D] rows (consecutive in (batch,
+// position, head) order, the layout of a projection's output): the register
+// kernels' rows, lanes and math, but each CTA walks its chunks of the grid-
+// stride order with the next kNRRingStages - 1 chunks already on their way into
+// a small ring of shared-memory stages (untiled bulk copies counted on one
+// mbarrier per stage), so its loads overlap its math without holding
+// registers.  Outputs are bit-identical to the register kernels'; the
+// backward's weight-gradient partials are per CTA over the same rows.
+// --------------------------------------------------------------------------
+
+// Chosen by A/B runs at config 4 (per launch, bf16): 2 stages of 64-row (forward)
+// and 32-row (backward) chunks.  3 and 4 stages, or 128-row forward / 64-row
+// backward chunks, leave fewer CTAs per SM and ran slower.
+constexpr int kNRRingStages = 2;
+constexpr int kNRRingFwdRows = 4;  // rows per lane per chunk
+constexpr int kNRRingBwdRows = 2;
+
+template <typename TE, int ROWS, int TENSORS>
+struct NRRing {
+  static constexpr int kRow = 64 * (int)sizeof(TE);  // bytes per row
+  static constexpr int kChunk = ROWS * kRow;          // bytes per chunk and tensor
+  static constexpr size_t kSums = TENSORS == 2 ? 16 * 64 * 4 : 0;  // backward: weight-gradient column sums
+  static constexpr size_t kSmem = (size_t)kNRRingStages * TENSORS * kChunk + kSums + kNRRingStages * 8;
+};
+
+// After an expired copy wait: record it and wait (bounded) for the copies still
+// in flight into this CTA's stages (chunks k0 .. k1 - 1), so none lands after exit.
+__device__ __forceinline__ void ring_drain(unsigned* status, uint64_t* bars, long long k0, long long k1) {
+  if (threadIdx.x == 0 && status) atomicOr(status, kFaultWaitExpired);
+  for (long long k = k0; k < k1; ++k)
+    (void)mbar_wait_bounded(bars + k % kNRRingStages, (uint32_t)((k / kNRRingStages) & 1));
+}
+
+// x (and dy) of ring chunk k of this CTA: rows [(blockIdx.x + k * gridDim.x) * ROWS, ...).
+template <typename TE, int ROWS, int TENSORS>
+__device__ __forceinline__ void ring_issue(uint8_t* ring, uint64_t* bars, const void* x, const void* dy, long long k,
+                                          long long rows_total) {
+  using R = NRRing<TE, ROWS, TENSORS>;
+  const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
+  const uint32_t bytes = (uint32_t)(min((long long)ROWS, rows_total - r0) * R::kRow);
+  uint64_t* bar = bars + k % kNRRingStages;
+  uint8_t* dst = ring + (k % kNRRingStages) * TENSORS * R::kChunk;
+  mbar_arrive_expect_tx(bar, TENSORS * bytes);
+  bulk_load(dst, static_cast<const uint8_t*>(x) + r0 * R::kRow, bytes, bar);
+  if (TENSORS == 2) bulk_load(dst + R::kChunk, static_cast<const uint8_t*>(dy) + r0 * R::kRow, bytes, bar);
+}
+
+template <typename TE>
+__global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_ring_kernel(const NormRopeParams p, const FastDiv fh,
+                                                                        const FastDiv fl) {
+  constexpr int ROWS = 16 * kNRRingFwdRows;
+  using R = NRRing<TE, ROWS, 1>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kNRRingStages * R::kChunk);
+  const int tid = threadIdx.x, l = tid & 7, grp = tid >> 3;
+  const long long rows_total = (long long)p.B * p.L * p.H;
+  const long long chunks = (rows_total + ROWS - 1) / ROWS;
+  const long long n = blockIdx.x < chunks ? (chunks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (tid == 0) {
+    for (int s = 0; s < kNRRingStages; ++s) mbar_init(bars + s, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (long long k = 0; k < n && k < kNRRingStages; ++k) ring_issue<TE, ROWS, 1>(smem, bars, p.x.ptr, nullptr, k, rows_total);
+  const NormRopeArgs a{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps};
+  const Frag w = nr_weights(p.w, l);
+  TE* y = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
+  for (long long k = 0; k < n; ++k) {
+    const bool ok = mbar_wait_bounded(bars + k % kNRRingStages, (uint32_t)((k / kNRRingStages) & 1));
+    if (__syncthreads_or(!ok)) {
+      ring_drain(p.status, bars, k, min(n, k + kNRRingStages));
+      return;
+    }
+    const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
+    const uint8_t* st = smem + (k % kNRRingStages) * R::kChunk;
+#pragma unroll
+    for (int i = 0; i < kNRRingFwdRows; ++i) {
+      // Rows past the tensor's end compute on stale stage bytes and store nothing.
+      const int rr = 16 * i + grp;
+      const long long row = r0 + rr;
+      const bool live = row < rows_total;
+      int b, pos, h;
+      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos, &h);
+      const Frag z = norm_rope_frag<TE>(FragIO<TE>::load(st + rr * R::kRow, l), l, w, a, pos, p.L, nullptr);
+      if (live) store_frag<TE, true>(y + nr_offset(p.y, b, pos, h), 1, 64, l, z);
+    }
+    __syncthreads();  // every thread is done with this stage
+    if (tid == 0 && k + kNRRingStages < n)
+      ring_issue<TE, ROWS, 1>(smem, bars, p.x.ptr, nullptr, k + kNRRingStages, rows_total);
+  }
+}
+
+// Backward: the register kernel's grid, with the same rows per CTA (chunks c,
+// c + grid, ...) and the same per-CTA partial rows, bit for bit.
+template <typename TE>
+__global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_ring_kernel(const NormRopeParams p, const FastDiv fh,
+                                                                        const FastDiv fl) {
+  constexpr int ROWS = 16 * kNRRingBwdRows;
+  using R = NRRing<TE, ROWS, 2>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* sums = reinterpret_cast<float*>(smem + kNRRingStages * 2 * R::kChunk);  // [16 row groups][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sums + 16 * 64);
+  const int tid = threadIdx.x, l = tid & 7, grp = tid >> 3;
+  const long long rows_total = (long long)p.B * p.L * p.H;
+  const long long chunks = (rows_total + ROWS - 1) / ROWS;
+  const long long n = blockIdx.x < chunks ? (chunks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (tid == 0) {
+    for (int s = 0; s < kNRRingStages; ++s) mbar_init(bars + s, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (long long k = 0; k < n && k < kNRRingStages; ++k)
+      ring_issue<TE, ROWS, 2>(smem, bars, p.x.ptr, p.dy.ptr, k, rows_total);
+  const NormRopeArgs a{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps};
+  const Frag w = nr_weights(p.w, l);
+  TE* dx = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
+  Frag dw = frag_zero();
+  for (long long k = 0; k < n; ++k) {
+    const bool ok = mbar_wait_bounded(bars + k % kNRRingStages, (uint32_t)((k / kNRRingStages) & 1));
+    if (__syncthreads_or(!ok)) {
+      // No partial row from this CTA: the fault word marks the result invalid.
+      ring_drain(p.status, bars, k, min(n, k + kNRRingStages));
+      return;
+    }
+    const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
+    const uint8_t* st = smem + (k % kNRRingStages) * 2 * R::kChunk;
+#pragma unroll
+    for (int i = 0; i < kNRRingBwdRows; ++i) {
+      const int rr = 16 * i + grp;
+      const long long row = r0 + rr;
+      const bool live = row < rows_total;
+      int b, pos, h;
+      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos, &h);
+      const Frag xv = FragIO<TE>::load(st + rr * R::kRow, l);
+      const float r = nr_rsqrt(fmaf(nr_row_dot(xv, xv), 1.f / 64.f, p.eps));
+      const Frag g = norm_rope_grad<TE>(FragIO<TE>::load(st + R::kChunk + rr * R::kRow, l), xv, r, l, w, a, pos,
+                                        p.L, dw, live);
+      if (live) store_frag<TE, true>(dx + nr_offset(p.y, b, pos, h), 1, 64, l, g);
+    }
+    __syncthreads();  // every thread is done with this stage
+    if (tid == 0 && k + kNRRingStages < n)
+      ring_issue<TE, ROWS, 2>(smem, bars, p.x.ptr, p.dy.ptr, k + kNRRingStages, rows_total);
+  }
+  // Fixed-order column sums of this CTA's row groups -> partial[blockIdx.x][j].
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sums[grp * 64 + 8 * l + 2 * i] = dw.v[i].x;
+    sums[grp * 64 + 8 * l + 2 * i + 1] = dw.v[i].y;
+  }
+  __syncthreads();
+  if (tid < 64) {
+    float acc = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) acc += sums[g * 64 + tid];
+    p.partial[(long long)blockIdx.x * 64 + tid] = acc;
+  }
+}
+
 // The vector path's preconditions (host side).
 bool nr_vec_ok(const TensorArg& t, int e) {
   if (reinterpret_cast<uintptr_t>(t.ptr) % 16 || t.sd != 1) return false;
@@ -403,8 +565,30 @@ bool nr_use64(const NormRopeParams& p, int e, bool backward) {
   return nr_vec_ok(p.x, e) && nr_vec_ok(p.y, e) && (!backward || nr_vec_ok(p.dy, e));
 }
 
+// Contiguous [B, L, H, D] rows of 64 channels: row r of the (batch, position,
+// head) order starts at element 64 r (a size-1 dimension may have any stride).
+bool nr_rows_contiguous(const TensorArg& t, const NormRopeParams& p) {
+  return t.sd == 1 && (p.H == 1 || t.sh == 64) && (p.L == 1 || t.sl == 64LL * p.H) &&
+         (p.B == 1 || t.sb == 64LL * p.H * p.L);
+}
+
 template <typename TE>
 int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
+  if (nr_use64(p, sizeof(TE), false) && nr_rows_contiguous(p.x, p)) {
+    // Every CTA resident at once (SMs x CTAs per SM), each walking several chunks.
+    auto kern = sbda_norm_rope64_fwd_ring_kernel<TE>;
+    const size_t smem = NRRing<TE, 16 * kNRRingFwdRows, 1>::kSmem;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return SBDA_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    const long long chunks = ((long long)p.B * p.L * p.H + 16 * kNRRingFwdRows - 1) / (16 * kNRRingFwdRows);
+    const long long cap = (long long)sm_count() * per_sm;
+    kern<<<(unsigned)(chunks < cap ? chunks : cap), 128, smem, st>>>(p, make_fastdiv((unsigned)p.H),
+                                                                    make_fastdiv((unsigned)p.L));
+    return cudaGetLastError() == cudaSuccess ? SBDA_OK : SBDA_ERR_CUDA;
+  }
   if (nr_use64(p, sizeof(TE), false)) {
     const long long rows = (long long)p.B * p.L * p.H;
     const long long grid = (rows + 16 * kNRFwdRows - 1) / (16 * kNRFwdRows);
@@ -422,7 +606,14 @@ int nr_forward(const NormRopeParams& p, unsigned blocks, cudaStream_t st) {
 
 template <typename TE>
 int nr_backward(const NormRopeParams& p, unsigned blocks, float* grad_w, cudaStream_t st) {
-  if (nr_use64(p, sizeof(TE), true)) {
+  if (nr_use64(p, sizeof(TE), true) && nr_rows_contiguous(p.x, p) && nr_rows_contiguous(p.dy, p)) {
+    // Same grid and rows per CTA as the register kernel below: the same partials.
+    auto kern = sbda_norm_rope64_bwd_ring_kernel<TE>;
+    const size_t smem = NRRing<TE, 16 * kNRRingBwdRows, 2>::kSmem;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return SBDA_ERR_CUDA;
+    kern<<<blocks, 128, smem, st>>>(p, make_fastdiv((unsigned)p.H), make_fastdiv((unsigned)p.L));
+  } else if (nr_use64(p, sizeof(TE), true)) {
     // `blocks` CTAs (a cap that depends on head_dim only, not the device) walk the rows, so
     // the partials and their summation order do not depend on the GPU.
     sbda_norm_rope64_bwd_kernel<TE><<<blocks, 128, 0, st>>>(p, make_fastdiv((unsigned)p.H),
@@ -479,6 +670,7 @@ NormRopeParams nr_params(const sbda_shape& s, const sbda_tensor& x, const sbda_t
   p.cos_t = cos_t;
   p.sin_t = sin_t;
   p.table_offset = table_offset;
+  p.status = status_ptr();
   return p;
 }
 

@@ -107,5 +107,34 @@ def test_norm_rope_backward_is_deterministic():
     assert torch.equal(grads[0][1], grads[1][1])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(1, 4099, 3), (2, 20000, 4), (3, 1, 5), (1, 300000, 4)])
+def test_norm_rope_contiguous_and_strided_paths_agree(dtype, shape):
+    """head_dim 64: contiguous [B, L, H, 64] rows take the kernels that stream rows through a
+    shared-memory ring, other vector layouts the kernels that load rows into registers.  Both run
+    the same rows, lanes and operations, so y, dx and the weight gradient agree bit for bit.  The
+    shapes cover a partial last chunk, a single partial chunk and many chunks per CTA."""
+    B, L, H = shape
+    g = torch.Generator(device="cuda").manual_seed(L + H)
+    x = (torch.randn(B, L, H, 64, device="cuda", generator=g) * 1.7).to(dtype)
+    dy = torch.randn(B, L, H, 64, device="cuda", generator=g).to(dtype)
+    w = torch.rand(64, device="cuda", generator=g) + 0.5
+    wide = torch.zeros(B, L, H, 128, device="cuda", dtype=dtype)
+    wide[..., 32:96] = x
+    results = []
+    for leaf in (x.clone().requires_grad_(), wide.clone().requires_grad_()):
+        xs = leaf if leaf.shape[-1] == 64 else leaf[..., 32:96]  # contiguous rows, then a strided view
+        wg = w.clone().requires_grad_()
+        y = sbda_b200.norm_rope(xs, wg, theta=1e6)
+        y.backward(dy)
+        dx = leaf.grad if leaf.shape[-1] == 64 else leaf.grad[..., 32:96]
+        results.append((y, dx, wg.grad))
+    (y1, dx1, dw1), (y2, dx2, dw2) = results
+    assert torch.equal(y1, y2)
+    assert torch.equal(dx1, dx2)
+    assert torch.equal(dw1, dw2)
+    assert sbda_b200.device_status(reset=True) == 0
+
+
 def test_norm_rope_fault_word_clean():
     assert sbda_b200.device_status(reset=True) == 0
