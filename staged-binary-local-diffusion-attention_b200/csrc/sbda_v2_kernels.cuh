@@ -1021,6 +1021,19 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
       auto rec = [&](int j, int src) {
         return *reinterpret_cast<const float2*>((j < 4 ? Ea + 8 * j : Eb + 8 * (j - 4)) + 2 * src);
       };
+      // NR: the group's four raw k rows, all loaded before this phase's first dK/dV
+      // store.  A load placed after a store it may alias (as far as the compiler
+      // knows) cannot move above it, so loads issued per key each wait out their
+      // own round trip to L2.
+      RowWords<TE> kraw[4];
+      if constexpr (NR && !is_pre) {
+        const TE* kb = reinterpret_cast<const TE*>(p.k.ptr) + (long long)b * p.k.sb + (long long)hk * p.k.sh;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = j0 + r0 + i;
+          kraw[i] = load_row_words<TE>(kb + (long long)min(j, p.L - 1) * p.k.sl, p.D, l, j < p.L);
+        }
+      }
       Frag q1 = FragIO<TE>::load(Qs + (r0 + 1) * P, l), d1 = FragIO<TE>::load(Ds + (r0 + 1) * P, l);
       Frag q0 = FragIO<TE>::load(Qs + r0 * P, l), d0 = FragIO<TE>::load(Ds + r0 * P, l);
 #pragma unroll
@@ -1064,9 +1077,7 @@ __global__ void __launch_bounds__(kThreads, NR ? 2 : 3) sbda_bwd_v2_kernel(const
           if constexpr (NR) {
             // dK of the raw row: RoPE transpose and RMSNorm Jacobian on the raw k,
             // re-read from global memory (the slot holding it is being refilled).
-            const TE* kb = reinterpret_cast<const TE*>(p.k.ptr) + (long long)b * p.k.sb + (long long)hk * p.k.sh;
-            const RowWords<TE> kw = load_row_words<TE>(kb + (long long)min(j, p.L - 1) * p.k.sl, p.D, l, j < p.L);
-            const Frag kx = FragIO<TE>::from_words(kw.w);
+            const Frag kx = FragIO<TE>::from_words(kraw[i].w);
             const float rk = nr_rsqrt(fmaf(nr_row_dot(kx, kx), 1.f / 64.f, p.nk.eps));
             ak = norm_rope_grad<TE>(ak, kx, rk, l, nr_weights(p.nk.w, l), p.nk, j, p.L, dwk, j < p.L);
           }
