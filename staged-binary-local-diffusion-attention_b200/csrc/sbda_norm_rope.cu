@@ -299,6 +299,7 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_kernel(const NormRop
   for (long long base = (long long)blockIdx.x * 16 * kNRFwdRows; base < rows_total;
        base += (long long)gridDim.x * 16 * kNRFwdRows) {
     RowWords<TE> in[kNRFwdRows];
+    RopeWords<TE> rw[kNRFwdRows];
     int pos[kNRFwdRows];
     long long yo[kNRFwdRows];
 #pragma unroll
@@ -309,10 +310,11 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_kernel(const NormRop
       nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos[i], &h);
       yo[i] = nr_offset(p.y, b, pos[i], h);
       in[i] = load_row_words<TE>(x + nr_offset(p.x, b, pos[i], h), 64, l, live);
+      rw[i] = rope_words<TE>(a, pos[i], p.L, l);
     }
 #pragma unroll
     for (int i = 0; i < kNRFwdRows; ++i) {
-      const Frag z = norm_rope_frag<TE>(FragIO<TE>::from_words(in[i].w), l, w, a, pos[i], p.L, nullptr);
+      const Frag z = norm_rope_frag_w<TE>(FragIO<TE>::from_words(in[i].w), l, w, a.eps, rw[i], nullptr);
       if (base + 16 * i + grp < rows_total) store_frag<TE, true>(y + yo[i], 1, 64, l, z);
     }
   }
@@ -325,6 +327,7 @@ constexpr int kNRBwdRows = 2;
 template <typename TE>
 struct NR64BwdRows {
   RowWords<TE> x[kNRBwdRows], g[kNRBwdRows];
+  RopeWords<TE> rw[kNRBwdRows];
   int pos[kNRBwdRows];
   long long dxo[kNRBwdRows];
 };
@@ -344,6 +347,7 @@ __device__ __forceinline__ void nr64_bwd_load(NR64BwdRows<TE>& r, const NormRope
     r.dxo[i] = nr_offset(p.y, b, r.pos[i], h);
     r.x[i] = load_row_words<TE>(x + nr_offset(p.x, b, r.pos[i], h), 64, l, live);
     r.g[i] = load_row_words<TE>(dy + nr_offset(p.dy, b, r.pos[i], h), 64, l, live);
+    r.rw[i] = rope_words<TE>(NormRopeArgs{p.w, p.cos_t, p.sin_t, p.table_offset, p.eps}, r.pos[i], p.L, l);
   }
 }
 
@@ -369,8 +373,7 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_kernel(const NormRop
       const bool live = base + 16 * i + grp < rows_total;
       const Frag xv = FragIO<TE>::from_words(cur.x[i].w);
       const float r = nr_rsqrt(fmaf(nr_row_dot(xv, xv), 1.f / 64.f, p.eps));
-      const Frag g =
-          norm_rope_grad<TE>(FragIO<TE>::from_words(cur.g[i].w), xv, r, l, w, a, cur.pos[i], p.L, dw, live);
+      const Frag g = norm_rope_grad_w<TE>(FragIO<TE>::from_words(cur.g[i].w), xv, r, l, w, cur.rw[i], dw, live);
       if (live) store_frag<TE, true>(dx + cur.dxo[i], 1, 64, l, g);
     }
   }
@@ -459,23 +462,31 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_fwd_ring_kernel(const No
   const Frag w = nr_weights(p.w, l);
   TE* y = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
   for (long long k = 0; k < n; ++k) {
+    // The chunk's coordinates and table words first: they overlap the stage's wait.
+    const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
+    int pos[kNRRingFwdRows];
+    long long yo[kNRRingFwdRows];
+    RopeWords<TE> rw[kNRRingFwdRows];
+#pragma unroll
+    for (int i = 0; i < kNRRingFwdRows; ++i) {
+      const long long row = r0 + 16 * i + grp;
+      int b, h;
+      nr_coords((unsigned)(row < rows_total ? row : rows_total - 1), fh, fl, &b, &pos[i], &h);
+      yo[i] = nr_offset(p.y, b, pos[i], h);
+      rw[i] = rope_words<TE>(a, pos[i], p.L, l);
+    }
     const bool ok = mbar_wait_bounded(bars + k % kNRRingStages, (uint32_t)((k / kNRRingStages) & 1));
     if (__syncthreads_or(!ok)) {
       ring_drain(p.status, bars, k, min(n, k + kNRRingStages));
       return;
     }
-    const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
     const uint8_t* st = smem + (k % kNRRingStages) * R::kChunk;
 #pragma unroll
     for (int i = 0; i < kNRRingFwdRows; ++i) {
       // Rows past the tensor's end compute on stale stage bytes and store nothing.
       const int rr = 16 * i + grp;
-      const long long row = r0 + rr;
-      const bool live = row < rows_total;
-      int b, pos, h;
-      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos, &h);
-      const Frag z = norm_rope_frag<TE>(FragIO<TE>::load(st + rr * R::kRow, l), l, w, a, pos, p.L, nullptr);
-      if (live) store_frag<TE, true>(y + nr_offset(p.y, b, pos, h), 1, 64, l, z);
+      const Frag z = norm_rope_frag_w<TE>(FragIO<TE>::load(st + rr * R::kRow, l), l, w, a.eps, rw[i], nullptr);
+      if (r0 + rr < rows_total) store_frag<TE, true>(y + yo[i], 1, 64, l, z);
     }
     __syncthreads();  // every thread is done with this stage
     if (tid == 0 && k + kNRRingStages < n)
@@ -510,26 +521,34 @@ __global__ void __launch_bounds__(128) sbda_norm_rope64_bwd_ring_kernel(const No
   TE* dx = reinterpret_cast<TE*>(const_cast<void*>(p.y.ptr));
   Frag dw = frag_zero();
   for (long long k = 0; k < n; ++k) {
+    // The chunk's coordinates and table words first: they overlap the stage's wait.
+    const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
+    long long dxo[kNRRingBwdRows];
+    RopeWords<TE> rw[kNRRingBwdRows];
+#pragma unroll
+    for (int i = 0; i < kNRRingBwdRows; ++i) {
+      const long long row = r0 + 16 * i + grp;
+      int b, pos, h;
+      nr_coords((unsigned)(row < rows_total ? row : rows_total - 1), fh, fl, &b, &pos, &h);
+      dxo[i] = nr_offset(p.y, b, pos, h);
+      rw[i] = rope_words<TE>(a, pos, p.L, l);
+    }
     const bool ok = mbar_wait_bounded(bars + k % kNRRingStages, (uint32_t)((k / kNRRingStages) & 1));
     if (__syncthreads_or(!ok)) {
       // No partial row from this CTA: the fault word marks the result invalid.
       ring_drain(p.status, bars, k, min(n, k + kNRRingStages));
       return;
     }
-    const long long r0 = ((long long)blockIdx.x + k * gridDim.x) * ROWS;
     const uint8_t* st = smem + (k % kNRRingStages) * 2 * R::kChunk;
 #pragma unroll
     for (int i = 0; i < kNRRingBwdRows; ++i) {
       const int rr = 16 * i + grp;
-      const long long row = r0 + rr;
-      const bool live = row < rows_total;
-      int b, pos, h;
-      nr_coords((unsigned)(live ? row : rows_total - 1), fh, fl, &b, &pos, &h);
+      const bool live = r0 + rr < rows_total;
       const Frag xv = FragIO<TE>::load(st + rr * R::kRow, l);
       const float r = nr_rsqrt(fmaf(nr_row_dot(xv, xv), 1.f / 64.f, p.eps));
-      const Frag g = norm_rope_grad<TE>(FragIO<TE>::load(st + R::kChunk + rr * R::kRow, l), xv, r, l, w, a, pos,
-                                        p.L, dw, live);
-      if (live) store_frag<TE, true>(dx + nr_offset(p.y, b, pos, h), 1, 64, l, g);
+      const Frag g =
+          norm_rope_grad_w<TE>(FragIO<TE>::load(st + R::kChunk + rr * R::kRow, l), xv, r, l, w, rw[i], dw, live);
+      if (live) store_frag<TE, true>(dx + dxo[i], 1, 64, l, g);
     }
     __syncthreads();  // every thread is done with this stage
     if (tid == 0 && k + kNRRingStages < n)

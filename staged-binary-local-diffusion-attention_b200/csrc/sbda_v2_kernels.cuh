@@ -149,17 +149,39 @@ __device__ __forceinline__ const TE* nr_table_row(const void* table, const NormR
   return reinterpret_cast<const TE*>(table) + (a.table_offset + p) * 32;
 }
 
-// Normalised and rotated channels of one lane (fp32 values of the element-type
-// results); r_out receives the row's rsqrt (the backward's Jacobian needs it).
+// The lane's cos and sin table words of one position (its 8 entries of each:
+// channels 8 (l & 3) .. 8 (l & 3) + 7 of the half-width table row).  Loading
+// them apart from their use lets callers issue the loads early: the table is
+// too large to stay in L1, and a load issued just before its use puts a round
+// trip to L2 on the row's dependency chain.
 template <typename TE>
-__device__ __forceinline__ Frag norm_rope_frag(const Frag& x, int l, const Frag& w, const NormRopeArgs& a, int pos,
-                                               int L, float* r_out) {
+struct RopeWords {
+  uint4 c[FragIO<TE>::kLaneBytes / 16], s[FragIO<TE>::kLaneBytes / 16];
+};
+
+template <typename TE>
+__device__ __forceinline__ RopeWords<TE> rope_words(const NormRopeArgs& a, int pos, int L, int l) {
+  const uint4* ct = reinterpret_cast<const uint4*>(nr_table_row<TE>(a.cos_t, a, pos, L) + 8 * (l & 3));
+  const uint4* st = reinterpret_cast<const uint4*>(nr_table_row<TE>(a.sin_t, a, pos, L) + 8 * (l & 3));
+  RopeWords<TE> rw;
+#pragma unroll
+  for (int i = 0; i < FragIO<TE>::kLaneBytes / 16; ++i) {
+    rw.c[i] = __ldg(ct + i);
+    rw.s[i] = __ldg(st + i);
+  }
+  return rw;
+}
+
+// Normalised and rotated channels of one lane (fp32 values of the element-type
+// results) from the position's table words; r_out receives the row's rsqrt
+// (the backward's Jacobian needs it).
+template <typename TE>
+__device__ __forceinline__ Frag norm_rope_frag_w(const Frag& x, int l, const Frag& w, float eps,
+                                                 const RopeWords<TE>& rw, float* r_out) {
   const unsigned full = 0xffffffffu;
-  const float r = nr_rsqrt(fmaf(nr_row_dot(x, x), 1.f / 64.f, a.eps));
+  const float r = nr_rsqrt(fmaf(nr_row_dot(x, x), 1.f / 64.f, eps));
   if (r_out) *r_out = r;
   const float2 rr = make_float2(r, r);
-  const TE* ct = nr_table_row<TE>(a.cos_t, a, pos, L) + 8 * (l & 3);
-  const TE* st = nr_table_row<TE>(a.sin_t, a, pos, L) + 8 * (l & 3);
   if constexpr (sizeof(TE) == 2) {
     using Ops = PackedOps<TE>;
     uint32_t y[4], z[4];
@@ -169,8 +191,7 @@ __device__ __forceinline__ Frag norm_rope_frag(const Frag& x, int l, const Frag&
       const float2 yw = mul2(n, w.v[i]);
       y[i] = Elem<TE>::pack2(yw.x, yw.y);
     }
-    const uint4 cw = __ldg(reinterpret_cast<const uint4*>(ct));
-    const uint4 sw = __ldg(reinterpret_cast<const uint4*>(st));
+    const uint4 cw = rw.c[0], sw = rw.s[0];
     const uint32_t c[4] = {cw.x, cw.y, cw.z, cw.w}, s[4] = {sw.x, sw.y, sw.z, sw.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -181,8 +202,8 @@ __device__ __forceinline__ Frag norm_rope_frag(const Frag& x, int l, const Frag&
     const uint4 zw = make_uint4(z[0], z[1], z[2], z[3]);
     return FragIO<TE>::from_words(&zw);
   } else {
-    const float4 c0 = __ldg(reinterpret_cast<const float4*>(ct)), c1 = __ldg(reinterpret_cast<const float4*>(ct + 4));
-    const float4 s0 = __ldg(reinterpret_cast<const float4*>(st)), s1 = __ldg(reinterpret_cast<const float4*>(st + 4));
+    const float4 c0 = *reinterpret_cast<const float4*>(&rw.c[0]), c1 = *reinterpret_cast<const float4*>(&rw.c[1]);
+    const float4 s0 = *reinterpret_cast<const float4*>(&rw.s[0]), s1 = *reinterpret_cast<const float4*>(&rw.s[1]);
     const float2 c[4] = {make_float2(c0.x, c0.y), make_float2(c0.z, c0.w), make_float2(c1.x, c1.y),
                          make_float2(c1.z, c1.w)};
     const float2 s[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
@@ -199,8 +220,16 @@ __device__ __forceinline__ Frag norm_rope_frag(const Frag& x, int l, const Frag&
   }
 }
 
+template <typename TE>
+__device__ __forceinline__ Frag norm_rope_frag(const Frag& x, int l, const Frag& w, const NormRopeArgs& a, int pos,
+                                               int L, float* r_out) {
+  return norm_rope_frag_w<TE>(x, l, w, a.eps, rope_words<TE>(a, pos, L, l), r_out);
+}
+
 // Rows [0, n) of a staged region starting at local position p0, normalised and
-// rotated in place by the CTA's row groups.  The trip count is the same for
+// rotated in place by the CTA's row groups.  (Fetching each iteration's table
+// words during the iteration before measured slower in both fused kernels.)
+// The trip count is the same for
 // every row group (the helpers shuffle across the whole warp): groups past the
 // end recompute row n - 1 and store nothing.
 template <typename TE, int P>
@@ -229,22 +258,10 @@ __device__ __forceinline__ void norm_rope_smem_rows(uint8_t* base, int n, int p0
 //   g_j = dz_j c_j + dz_{j+32} s_j,   g_{j+32} = dz_{j+32} c_j - dz_j s_j,
 //   dx  = r (g w) - x r^3 sum(g w x) / 64.
 template <typename TE>
-__device__ __forceinline__ Frag norm_rope_grad(const Frag& dz, const Frag& x, float r, int l, const Frag& w,
-                                               const NormRopeArgs& a, int pos, int L, Frag& dw, bool acc) {
+__device__ __forceinline__ Frag norm_rope_grad_w(const Frag& dz, const Frag& x, float r, int l, const Frag& w,
+                                                 const RopeWords<TE>& rw, Frag& dw, bool acc) {
   const unsigned full = 0xffffffffu;
-  const TE* ct = nr_table_row<TE>(a.cos_t, a, pos, L) + 8 * (l & 3);
-  const TE* st = nr_table_row<TE>(a.sin_t, a, pos, L) + 8 * (l & 3);
-  Frag c, s;
-  if constexpr (sizeof(TE) == 2) {
-    const uint4 cw = __ldg(reinterpret_cast<const uint4*>(ct)), sw = __ldg(reinterpret_cast<const uint4*>(st));
-    c = FragIO<TE>::from_words(&cw);
-    s = FragIO<TE>::from_words(&sw);
-  } else {
-    const uint4 cw[2] = {__ldg(reinterpret_cast<const uint4*>(ct)), __ldg(reinterpret_cast<const uint4*>(ct + 4))};
-    const uint4 sw[2] = {__ldg(reinterpret_cast<const uint4*>(st)), __ldg(reinterpret_cast<const uint4*>(st + 4))};
-    c = FragIO<TE>::from_words(cw);
-    s = FragIO<TE>::from_words(sw);
-  }
+  const Frag c = FragIO<TE>::from_words(rw.c), s = FragIO<TE>::from_words(rw.s);
   const float sg = l < 4 ? 1.f : -1.f;
   const float2 rr = make_float2(r, r);
   Frag u;
@@ -261,6 +278,12 @@ __device__ __forceinline__ Frag norm_rope_grad(const Frag& dz, const Frag& x, fl
 #pragma unroll
   for (int i = 0; i < 4; ++i) dx.v[i] = fma2(x.v[i], kk, mul2(u.v[i], rr));
   return dx;
+}
+
+template <typename TE>
+__device__ __forceinline__ Frag norm_rope_grad(const Frag& dz, const Frag& x, float r, int l, const Frag& w,
+                                               const NormRopeArgs& a, int pos, int L, Frag& dw, bool acc) {
+  return norm_rope_grad_w<TE>(dz, x, r, l, w, rope_words<TE>(a, pos, L, l), dw, acc);
 }
 
 // Per-CTA weight-gradient partials: the 16 row groups' fp32 sums (q then k) go
@@ -336,6 +359,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
 
   const int a = grp * 4;
   RowWords<TE> qw[4];
+  RopeWords<TE> qrw[4];  // NR: table words of the group's Q rows
   if constexpr (TMA) {
     if (tid == 0) {
       mbar_init(bar, 1);
@@ -369,12 +393,13 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
         }
       }
     }
-    // Q rows of this group, in flight while the K/V copies land.
+    // Q rows of this group (and, NR, their table words), in flight while the K/V copies land.
     const TE* qb = reinterpret_cast<const TE*>(p.q.ptr) + (long long)b * p.q.sb + (long long)h * p.q.sh;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int pos = i0 + a + i;
       qw[i] = load_row_words<TE>(qb + (long long)min(pos, p.L - 1) * p.q.sl, p.D, l, pos < p.L);
+      if constexpr (NR) qrw[i] = rope_words<TE>(p.nq, pos, p.L, l);
     }
     const bool ok = mbar_wait_bounded(bar, 0);
     if (__syncthreads_or(!ok)) {
@@ -417,7 +442,7 @@ __global__ void __launch_bounds__(kThreads) sbda_fwd_v2_kernel(const __grid_cons
     const int r = a + i, pos = i0 + r;
     const int pg = p.sh.pos0 + pos;  // global position: source masks
     Frag q = TMA ? FragIO<TE>::from_words(qw[i].w) : FragIO<TE>::load(Qs + r * P, l);
-    if constexpr (NR) q = norm_rope_frag<TE>(q, l, wq, p.nq, pos, p.L, nullptr);
+    if constexpr (NR) q = norm_rope_frag_w<TE>(q, l, wq, p.nq.eps, qrw[i], nullptr);
     const Frag k0 = FragIO<TE>::load(Kn + (r + lead) * P, l);
     const Frag v0 = FragIO<TE>::load(Vn + (r + lead) * P, l);
     if constexpr (LPR == 8) {
