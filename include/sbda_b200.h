@@ -32,6 +32,12 @@
  *  - No entry point allocates device memory, synchronises, or keeps state
  *    between calls.  Work is enqueued on `stream` (a cudaStream_t; NULL is
  *    the legacy default stream).
+ *  - The attention kernels are launched with programmatic stream
+ *    serialization and let the next kernel on the stream start early.  A
+ *    kernel that the caller launches right after a call with that same launch
+ *    attribute must wait on its grid dependency (cudaGridDependencySynchronize)
+ *    before it reads the call's outputs; ordinary launches, copies and events
+ *    see the call complete as usual.
  *  - Return value: SBDA_OK or an error code; sbda_b200_status_string() names it.
  */
 #ifndef SBDA_B200_H_
